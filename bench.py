@@ -1,0 +1,380 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 attention backend (decode hot path).
+
+Metric: decode-attention HBM GB/s. One step = one decode
+batch of config 2 through all 28 layers of Qwen3-0.6B attention: per layer the
+fused RoPE + KV store of the B new tokens and paged split-KV decode attention
+over the cached context (AttentionLayer.__call__, reference layers.py:103-111).
+
+  value  = algorithmic bytes of the step / device time, inputs resident in HBM
+           (each layer's KV working set, ~560 MB, exceeds the 126 MB L2)
+  e2e    = the same metric through the public API with HOST buffers: per step
+           prepare_metadata (host numpy + plan + one H2D copy), H2D of every
+           layer's q/k/v from pinned memory, the 28 AttentionLayer calls, and a
+           D2H read of every layer's output
+  roofline: decode call (decode kernel + split merge) per launch, CUDA events
+  cpu_baseline: the CPU oracle port (torch, naive gather + masked SDPA) on one
+           layer of the same batch (rank 0, N = 1 only)
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+N > 1 is launched by torchrun: every rank runs its own config-2 batch on its
+own GPU (request-partitioned weak scaling, no data-path collective).
+"""
+
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "mini-sglang-mlx_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "decode-attn HBM GB/s (% of peak) + end-to-end output tok/s at 1/2/4/8 B200"
+UNIT = "GB/s"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+# ------------------------------------------------------------------ clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.file = None
+
+    def start(self):
+        try:
+            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.file.flush()
+        self.file.seek(0)
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.file.read().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sms.append(float(parts[1]))
+                maxes.append(float(parts[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        os.unlink(self.file.name)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+# ------------------------------------------------------------------ workload
+def decode_bytes(lens: np.ndarray, P: int, Hq: int, Hkv: int, D: int, es: int) -> int:
+    """Algorithmic bytes of one decode call: K and V rows of every cached token, q, o, page ids."""
+    L = int(lens.sum())
+    pages = int(((lens + P - 1) // P).sum())
+    B = len(lens)
+    return L * Hkv * D * es * 2 + 2 * B * Hq * D * es + 4 * pages + 4 * (B + 1)
+
+
+def rope_store_bytes(T: int, Hq: int, Hkv: int, D: int, es: int) -> int:
+    """q,k read+write, v read, k,v pool write, positions + out_loc."""
+    return T * (Hq + Hkv) * D * es * 2 + T * Hkv * D * es * 3 + 8 * T
+
+
+def cpu_sample(lens, page_table, P, Hq, Hkv, D, num_slots, steps, warmup, seed):
+    """Time the oracle port (naive gather + masked SDPA, torch CPU fp32 math on bf16 pools)."""
+    import torch
+
+    from oracle.cpu_naive import naive_decode_torch
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    g = torch.Generator().manual_seed(seed)
+    k_pool = torch.randn((num_slots, Hkv, D), generator=g).to(torch.bfloat16)
+    v_pool = torch.randn((num_slots, Hkv, D), generator=g).to(torch.bfloat16)
+    q = torch.randn((len(lens), Hq, D), generator=g).to(torch.bfloat16)
+    rows = np.arange(len(lens))
+    times = []
+    for i in range(warmup + steps):
+        t0 = time.perf_counter()
+        naive_decode_torch(q, k_pool, v_pool, page_table, rows, lens, D ** -0.5)
+        dt = time.perf_counter() - t0
+        if i >= warmup:
+            times.append(dt)
+    per_call = float(np.mean(times))
+    gbs = decode_bytes(lens, P, Hq, Hkv, D, 2) / per_call / 1e9
+    return gbs, per_call, torch.get_num_threads()
+
+
+# ------------------------------------------------------------------ reference arm
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from minisgl_b200 import workloads as W
+
+    c = W.CONFIG2
+    pb = W.config2_batch(seed=args.seed)
+    steps = max(1, min(args.steps, 20))
+    warm = max(0, min(args.warmup, 3))
+    gbs, per_call, cores = cpu_sample(pb.lens, pb.page_table, pb.page_size, c["Hq"], c["Hkv"], c["D"],
+                                      c["num_slots"], steps, warm, args.seed)
+    sample = (f"one layer of config 2 per step (B={pb.batch_size}, sum L={int(pb.lens.sum())}, bf16 pools, "
+              f"naive gather+mask+SDPA in fp32 on {cores} threads); {steps} timed steps")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "steps": steps, "warmup": warm, "ms_per_step": round(per_call * 1e3, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": "config2: batched paged decode, 16q/8kv/128, page 16, B=128, L~U[100,2048]",
+                   "kind": "cpu oracle port (MLX CPU path unavailable on this box)"},
+        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ------------------------------------------------------------------ our arm
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+
+    from minisgl_b200 import (AttentionLayer, Batch, Context, MHAKVCache, Req, set_global_ctx)
+    from minisgl_b200 import workloads as W
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.config import qwen3_0_6b
+    from minisgl_b200.core import batch_positions_out_loc
+
+    c = W.CONFIG2
+    cfg = qwen3_0_6b()
+    Lyr, Hq, Hkv, D, P, N = c["layers"], cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim, c["page_size"], c["num_slots"]
+    pb = W.config2_batch(seed=args.seed + 1000 * rank)
+    B = pb.batch_size
+
+    kv = MHAKVCache(Lyr, N, Hkv, D, torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(args.seed + 17 * rank)
+    for l in range(Lyr):
+        kv.k[l].normal_(generator=gen)
+        kv.v[l].normal_(generator=gen)
+    ctx = Context(page_size=P)
+    ctx.page_table = pb.page_table
+    ctx.kv_cache = kv
+    be = B200AttnBackend(cfg, kv, pb.page_table, page_size=P)
+    ctx.attn_backend = be
+    set_global_ctx(ctx)
+    layers = [AttentionLayer(l, Hq, Hkv, D, cfg.rotary_config) for l in range(Lyr)]
+
+    # decode batch: the new token of request b sits at position lens[b]-1 (its slot is allocated)
+    reqs = []
+    for b in range(B):
+        L = int(pb.lens[b])
+        r = Req(np.zeros(L - 1, np.int32), table_idx=int(pb.rows[b]), cached_len=0, output_len=2)
+        r.complete_one()  # cached_len = L-1, device_len = L
+        reqs.append(r)
+    batch = Batch(reqs, "decode")
+    pos, loc = batch_positions_out_loc(batch, pb.page_table)
+    batch.positions = torch.from_numpy(pos).to(dev)
+    batch.out_loc = torch.from_numpy(loc).to(dev)
+    be.prepare_metadata(batch)
+    meta = batch.attn_metadata
+
+    # per-layer inputs: q [B, Hq, D] contiguous, new k/v rows interleaved [B, 2, Hkv, D]
+    q_all = torch.randn((Lyr, B, Hq, D), device=dev, generator=gen).to(torch.bfloat16)
+    kv_all = torch.randn((Lyr, B, 2, Hkv, D), device=dev, generator=gen).to(torch.bfloat16)
+    views = [(q_all[l], kv_all[l, :, 0], kv_all[l, :, 1]) for l in range(Lyr)]
+
+    dec_events = []
+
+    def step(record=False):
+        with ctx.forward_batch(batch):
+            for l in range(Lyr):
+                q, k, v = views[l]
+                layers[l].rotary.rope_store_(q, k, v, batch.positions, batch.out_loc, kv, l)
+                if record:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e0.record()
+                    be.forward(q, k, v, l, batch)
+                    e1.record()
+                    dec_events.append((e0, e1))
+                else:
+                    be.forward(q, k, v, l, batch)
+
+    # ---------------- device-resident timing
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clocks = ClockSampler(local)
+    clocks.start()
+    t0 = torch.cuda.Event(enable_timing=True)
+    t1 = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    t0.record()
+    for _ in range(args.steps):
+        step(record=True)
+    t1.record()
+    torch.cuda.synchronize()
+    clk = clocks.stop()
+    ms = t0.elapsed_time(t1) / args.steps
+    dec_ms = [a.elapsed_time(b) for a, b in dec_events]
+
+    # ---------------- end to end through the public API with host buffers
+    host_q = torch.empty(q_all.shape, dtype=torch.bfloat16, pin_memory=True)
+    host_q.copy_(q_all.cpu())
+    host_kv = torch.empty(kv_all.shape, dtype=torch.bfloat16, pin_memory=True)
+    host_kv.copy_(kv_all.cpu())
+    host_out = torch.empty((Lyr, B, Hq * D), dtype=torch.bfloat16, pin_memory=True)
+    dev_q = torch.empty_like(q_all)
+    dev_kv = torch.empty_like(kv_all)
+    meta_bytes = [0]
+
+    def e2e_step():
+        be.prepare_metadata(batch)  # host numpy + plan + one pinned H2D copy
+        m = batch.attn_metadata
+        meta_bytes[0] = 4 * (m.kv_indptr.numel() + m.kv_indices.numel() + m.kv_last_page_len.numel()
+                             + m.cta_indptr.numel() + m.segs.numel() + m.merge_indptr.numel())
+        dev_q.copy_(host_q, non_blocking=True)
+        dev_kv.copy_(host_kv, non_blocking=True)
+        outs = []
+        with ctx.forward_batch(batch):
+            for l in range(Lyr):
+                outs.append(layers[l](dev_q[l], dev_kv[l, :, 0], dev_kv[l, :, 1]))
+        for l in range(Lyr):
+            host_out[l].copy_(outs[l], non_blocking=True)
+
+    for _ in range(max(args.warmup, 3)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = e0.elapsed_time(e1) / args.steps
+
+    # ---------------- reduce over ranks (max time, summed work)
+    dbytes = decode_bytes(pb.lens, P, Hq, Hkv, D, 2)
+    sbytes = rope_store_bytes(B, Hq, Hkv, D, 2)
+    step_bytes = Lyr * (dbytes + sbytes)
+    stats = torch.tensor([ms, e2e_ms, float(np.mean(dec_ms))], dtype=torch.float64, device=dev)
+    work = torch.tensor([float(step_bytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(work, op=dist.ReduceOp.SUM)
+    ms, e2e_ms, dec_avg = stats.tolist()
+    total_bytes = float(work.item())
+    value = total_bytes / (ms * 1e-3) / 1e9
+    e2e_value = total_bytes / (e2e_ms * 1e-3) / 1e9
+
+    peak, peak_kind = measured_peaks()
+    achieved = dbytes / (dec_avg * 1e-3) / 1e9
+    launches_per_step = Lyr * (2 + (1 if meta.n_partials > 0 else 0))
+
+    line = None
+    if rank == 0:
+        cpu = None
+        if world == 1 and not args.no_cpu_baseline:
+            sub = W.config2_batch(seed=args.seed)
+            gbs, per_call, cores = cpu_sample(sub.lens, sub.page_table, P, Hq, Hkv, D, N, 3, 1, args.seed)
+            cpu = {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port",
+                   "sample": f"1 layer of config 2 (B={B}, sum L={int(sub.lens.sum())}), mean of 3 calls, "
+                             f"torch CPU naive gather+mask+SDPA; MLX CPU unavailable on this box"}
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {
+                "workload": "config2: batched paged decode step, Qwen3-0.6B attention x28 layers "
+                            "(16q/8kv/128, bf16, page 16, pool 262144 slots/layer, B=128/GPU, L~U[100,2048], "
+                            "fragmented pages); per layer fused RoPE+KV store + split-KV decode",
+                "global_batch": B * world, "seq_len": "U[100,2048]", "parallelism": f"request-partitioned x{world}",
+                "l2": "inputs larger than L2 (each layer's ~560 MB KV working set > 126 MB L2)",
+                "sum_ctx_tokens_per_gpu": int(pb.lens.sum()),
+            },
+            "roofline": {
+                "bound": "hbm", "kernel": "decode_kernel+decode_merge_kernel (one b2a_decode call)",
+                "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
+                "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_avg, 5), "traffic": None,
+            },
+            "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
+                    "h2d_bytes_per_step": int((host_q.numel() + host_kv.numel()) * 2 + meta_bytes[0]),
+                    "d2h_bytes_per_step": int(host_out.numel() * 2), "ms_per_step": round(e2e_ms, 4)},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clk,
+        }
+        if cpu is not None:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,167 @@
+/*
+ * b200attn.h - C ABI of the B200 attention backend for mini-sglang-mlx.
+ *
+ * The library (libb200attn.so) replaces the reference's attention hot path:
+ * the KV-pool store, the rotary embedding applied in AttentionLayer, the
+ * shared prefill/extend attention and the paged decode attention. Every entry
+ * point takes plain device pointers, sizes and a CUDA stream (cudaStream_t
+ * passed as void*); nothing here knows about torch, MLX or Python objects.
+ *
+ * Conventions
+ *   - Status: every int-returning call returns B2A_OK (0) or a nonzero
+ *     B2A_ERR_* code; b2a_last_error() returns the message of the last failing
+ *     call made on this host thread.
+ *   - dtype: B2A_DTYPE_F32 or B2A_DTYPE_BF16 (B2A_DTYPE_F16 is accepted by the
+ *     store/rope kernels only). All activations and pools share one dtype.
+ *   - Layouts (row-major, innermost last):
+ *       q, out           [T, Hq, D]   (decode: T = B, one query row per request)
+ *       k, v (new rows)  [T, Hkv, D]  with an explicit token-row stride
+ *       k_pool, v_pool   [num_slots, Hkv, D] for ONE layer
+ *   - Paging: a page is page_size consecutive pool slots starting at a
+ *     multiple of page_size. kv_indptr[B+1] is a CSR over pages,
+ *     kv_indices[] holds page ids (slot / page_size) and kv_last_page_len[B]
+ *     the number of valid slots in each request's last page (NULL means every
+ *     last page is full). With
+ *     page_size == 1 this is exactly the token CSR of the reference's Metal
+ *     backend (kv_indptr = [0, cumsum(L)], kv_indices = slots).
+ *   - Bounds: every page id / slot is checked on the device against
+ *     num_slots; an out-of-range index skips the access and sets the watchdog
+ *     word (b2a_device_error) instead of faulting.
+ *   - Allocation: no entry point allocates device memory. Scratch comes from
+ *     a caller-provided workspace sized by the *_workspace_bytes queries.
+ *   - Threading: calls are re-entrant across streams; the host-side error
+ *     string is thread-local. Plans are pure host functions.
+ */
+#ifndef B200ATTN_H
+#define B200ATTN_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define B2A_ABI_VERSION 1
+
+#define B2A_DTYPE_F32 0
+#define B2A_DTYPE_BF16 1
+#define B2A_DTYPE_F16 2
+
+#define B2A_OK 0
+#define B2A_ERR_INVALID 1     /* bad argument (shape, pointer, alignment) */
+#define B2A_ERR_UNSUPPORTED 2 /* valid but not compiled (e.g. head_dim 96) */
+#define B2A_ERR_CUDA 3        /* CUDA launch/runtime error                 */
+#define B2A_ERR_WORKSPACE 4   /* workspace or plan capacity too small      */
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* b2a_last_error(void);
+
+/* B2A_ABI_VERSION of the loaded library. */
+int b2a_abi_version(void);
+
+/* Reads and clears the device-side watchdog word that bounded spin-waits
+ * set when they give up (0 = no error). Synchronises `stream`. */
+int b2a_device_error(void* stream, int* code_out);
+
+/* ------------------------------------------------------------------------
+ * KV-pool store.
+ * Replaces MHAKVCache.store_kv (python/minisgl_mlx/kvcache/pool.py:47-50):
+ *   k_pool[out_loc[t]] = k[t];  v_pool[out_loc[t]] = v[t]   for t < T.
+ * Byte-exact copy. out_loc entries must be unique and < num_slots.
+ * ------------------------------------------------------------------------ */
+int b2a_store_kv(const void* k, int64_t k_row_stride, const void* v, int64_t v_row_stride,
+                 const int32_t* out_loc, void* k_pool, void* v_pool, int64_t num_slots, int T,
+                 int Hkv, int D, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Fused rotary embedding + KV store.
+ * Replaces the first three lines of AttentionLayer.__call__
+ * (python/minisgl_mlx/layers.py:107-109): RotaryEmbedding (layers.py:45-56,
+ * mx.fast.rope with traditional=False) on q and k, then store_kv of the
+ * rotated k and the untouched v (kvcache/pool.py:47-50).
+ *   angle(t, i) = fl32(fl32(positions[t] * rope_scale) * inv_freq[i]),
+ *   i < rot_dim/2; pairs (i, i + rot_dim/2) are rotated, features >= rot_dim
+ *   pass through. q and k are rotated IN PLACE (row strides in elements).
+ * inv_freq: device float32[rot_dim/2] (base^(-2i/rot_dim), or 1/freqs for
+ * llama3 scaling). rot_dim == 0 disables the rotation (pure store);
+ * k_pool == v_pool == NULL disables the store (pure rope).
+ * ------------------------------------------------------------------------ */
+int b2a_rope_store(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* v,
+                   int64_t v_row_stride, const int32_t* positions, const int32_t* out_loc,
+                   void* k_pool, void* v_pool, int64_t num_slots, const float* inv_freq,
+                   float rope_scale, int rot_dim, int T, int Hq, int Hkv, int D, int dtype,
+                   void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged decode attention, drop-in form.
+ * Same inputs and meaning as paged_decode_attention
+ * (python/minisgl_mlx/attention/metal.py:112-131): one query row per request,
+ * kv_indptr[B+1] token CSR, kv_indices[] pool slots (page_size 1),
+ *   out[b, h] = softmax(scale * q[b,h] . K[idx]^T) . V[idx],
+ *   idx = kv_indices[kv_indptr[b] : kv_indptr[b+1]], kv head = h / (Hq/Hkv).
+ * One CTA per request, no split, no workspace. fp32 accumulation.
+ * ------------------------------------------------------------------------ */
+int b2a_paged_decode(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                     const int32_t* kv_indptr, const int32_t* kv_indices, int B, int Hq, int Hkv,
+                     int D, float scale, void* out, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
+ * Paged split-KV decode attention, production form.
+ * Replaces MetalAttnBackend.prepare_decode/forward_decode
+ * (python/minisgl_mlx/attention/metal.py:145-162) and the naive backend's
+ * forward_decode (attention/naive.py:50-60), which computes the same values.
+ *
+ * b2a_decode_plan (host only, no GPU): cuts the concatenated page stream of
+ * all requests into `num_ctas` near-equal contiguous ranges. Each range is a
+ * list of segments {request, first page index into kv_indices, n_tokens,
+ * out_slot}; out_slot == -1 writes the final output directly, otherwise the
+ * segment writes a partial (m, l, acc) that b2a_decode merges per request.
+ *   kv_indptr, kv_last_page_len : HOST int32 [B+1], [B] (NULL = full pages)
+ *   cta_indptr (out)            : int32 [num_ctas + 1] CSR over segments
+ *   segs (out)                  : int32 [seg_capacity * 4]
+ *   merge_indptr (out)          : int32 [B + 1] CSR over partial slots
+ * b2a_decode_num_ctas returns the persistent grid size the kernel wants on
+ * the current device for this head shape (SM count x resident CTAs).
+ * ------------------------------------------------------------------------ */
+int b2a_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,
+                    int page_size, int num_ctas, int32_t* cta_indptr, int32_t* segs,
+                    int seg_capacity, int32_t* merge_indptr, int* n_segs, int* n_partials);
+int b2a_decode_num_ctas(int Hq, int Hkv, int D, int dtype, int* num_ctas);
+size_t b2a_decode_workspace_bytes(int n_partials, int Hq, int D);
+int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+               const int32_t* kv_indices, int page_size, const int32_t* cta_indptr, const int32_t* segs, int num_ctas,
+               const int32_t* merge_indptr, int n_partials, int B, int Hq, int Hkv, int D,
+               float scale, void* workspace, size_t workspace_bytes, void* out, int dtype,
+               void* stream);
+
+/* ------------------------------------------------------------------------
+ * Ragged causal extend (prefill) attention over a paged prefix.
+ * Replaces BaseAttnBackend._prepare_prefill/_forward_prefill
+ * (python/minisgl_mlx/attention/base.py:107-142): request r owns query rows
+ * [qo_indptr[r], qo_indptr[r+1]) (Lq rows) and Lkv pool tokens described by
+ * its pages (the cached prefix followed by the rows just stored). Row i of r
+ * attends keys j <= Lkv - Lq + i (bottom-right causal, mx.fast SDPA
+ * mask="causal"; for Lq == 1 this is "no mask").
+ * b2a_extend_plan (host only) tiles every request into query tiles of
+ * b2a_extend_tile_q() rows and orders them longest-first:
+ *   work (out) : int32 [work_capacity * 4] = {request, q_tile_begin, q_tile_rows, 0}
+ * The kernel is chosen by dtype/shape: bf16 with D == 128 runs on tcgen05
+ * tensor cores (TMEM accumulators, TMA-fed tiles); every other supported
+ * shape runs a SIMT fp32-accumulating kernel.
+ * ------------------------------------------------------------------------ */
+int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int* tile_q);
+int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
+                    const int32_t* kv_last_page_len, int B, int page_size, int tile_q,
+                    int32_t* work, int work_capacity, int* n_work);
+int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+               const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
+               const int32_t* kv_last_page_len, int page_size, const int32_t* work, int n_work,
+               int T, int B, int Hq, int Hkv, int D, float scale, void* out, int dtype,
+               void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* B200ATTN_H */

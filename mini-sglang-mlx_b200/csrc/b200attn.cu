@@ -1,0 +1,517 @@
+// C ABI of the B200 attention backend: argument validation, host-side plans,
+// kernel configuration and dispatch. Declarations and contracts live in
+// include/b200attn.h; each kernel file names the reference code it replaces.
+#include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <string>
+#include <vector>
+
+#include "../../include/b200attn.h"
+#include "common.cuh"
+#include "decode.cuh"
+#include "extend_simt.cuh"
+#include "extend_tc.cuh"
+#include "rope_store.cuh"
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_err = buf;
+  return code;
+}
+
+int ok() {
+  g_err.clear();
+  return B2A_OK;
+}
+
+int check_launch(const char* what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "%s: CUDA error %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int ilog2_exact(int x) {
+  if (x <= 0 || (x & (x - 1)) != 0) return -1;
+  int l = 0;
+  while ((1 << l) < x) ++l;
+  return l;
+}
+
+size_t dtype_size(int dtype) {
+  switch (dtype) {
+    case B2A_DTYPE_F32:
+      return 4;
+    case B2A_DTYPE_BF16:
+    case B2A_DTYPE_F16:
+      return 2;
+    default:
+      return 0;
+  }
+}
+
+// Calls f(T{}) for the element type of `dtype`; f returns an int status.
+template <bool AllowF16, typename F>
+int with_dtype(int dtype, F&& f) {
+  switch (dtype) {
+    case B2A_DTYPE_F32:
+      return f(float{});
+    case B2A_DTYPE_BF16:
+      return f(__nv_bfloat16{});
+    case B2A_DTYPE_F16:
+      if constexpr (AllowF16) return f(__half{});
+      return fail(B2A_ERR_UNSUPPORTED, "fp16 is supported by the store/rope kernels only");
+    default:
+      return fail(B2A_ERR_INVALID, "unknown dtype code %d", dtype);
+  }
+}
+
+template <int D, typename F>
+int with_g(int G, F&& f) {
+  switch (G) {
+    case 1:
+      return f(std::integral_constant<int, 1>{});
+    case 2:
+      return f(std::integral_constant<int, 2>{});
+    case 4:
+      return f(std::integral_constant<int, 4>{});
+    case 8:
+      return f(std::integral_constant<int, 8>{});
+    default:
+      return fail(B2A_ERR_UNSUPPORTED, "GQA group size %d not compiled (1, 2, 4, 8)", G);
+  }
+}
+
+template <typename F>
+int with_d(int D, F&& f) {
+  switch (D) {
+    case 64:
+      return f(std::integral_constant<int, 64>{});
+    case 128:
+      return f(std::integral_constant<int, 128>{});
+    case 256:
+      return f(std::integral_constant<int, 256>{});
+    default:
+      return fail(B2A_ERR_UNSUPPORTED, "head_dim %d not compiled (64, 128, 256)", D);
+  }
+}
+
+int check_heads(int Hq, int Hkv, int D) {
+  if (Hq <= 0 || Hkv <= 0 || D <= 0) return fail(B2A_ERR_INVALID, "head counts and head_dim must be > 0");
+  if (Hq % Hkv != 0) return fail(B2A_ERR_INVALID, "Hq (%d) must be a multiple of Hkv (%d)", Hq, Hkv);
+  if (D % 32 != 0) return fail(B2A_ERR_INVALID, "head_dim %d must be a multiple of 32", D);
+  return B2A_OK;
+}
+
+// ------------------------------------------------------------ decode config
+struct DecodeCfg {
+  int TS, NSTAGE, WPH, NCW;
+  uint32_t row_bytes, stage_bytes;
+  size_t smem;
+};
+
+constexpr size_t kSmemLimit = 232448;  // opt-in dynamic shared memory per block (sm_100)
+
+int decode_config(int Hq, int Hkv, int D, size_t es, DecodeCfg& c) {
+  if (Hkv > 8 || 8 % Hkv != 0)
+    return fail(B2A_ERR_UNSUPPORTED, "decode supports Hkv in {1, 2, 4, 8}, got %d", Hkv);
+  const int G = Hq / Hkv;
+  c.WPH = 8 / Hkv;
+  c.NCW = 8;
+  c.row_bytes = (uint32_t)(Hkv * D * es);
+  int TS = 64;
+  while (TS > 1 && 2ull * TS * c.row_bytes > 65536ull) TS >>= 1;
+  for (;;) {
+    c.TS = TS;
+    c.stage_bytes = (uint32_t)TS * c.row_bytes;
+    const b2a::DecodeSmem fixed = b2a::decode_smem_layout(0, 0, c.NCW, c.WPH, G, D);
+    const size_t avail = kSmemLimit - fixed.total - 256;
+    int ns = (int)std::min<size_t>(4, avail / (2ull * c.stage_bytes));
+    if (ns >= 2 || TS == 1) {
+      c.NSTAGE = std::max(ns, 1);
+      break;
+    }
+    TS >>= 1;
+  }
+  c.smem = b2a::decode_smem_layout(c.NSTAGE, c.stage_bytes, c.NCW, c.WPH, G, D).total;
+  if (c.smem > kSmemLimit) return fail(B2A_ERR_UNSUPPORTED, "decode config does not fit in shared memory");
+  return B2A_OK;
+}
+
+template <typename T, int D, int G>
+int decode_launch(const b2a::DecodeArgs& a, const DecodeCfg& c, int grid, cudaStream_t st) {
+  auto kern = b2a::decode_kernel<T, D, G>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
+  if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "decode: set smem attribute: %s", cudaGetErrorString(e));
+  kern<<<grid, (c.NCW + 1) * 32, c.smem, st>>>(a);
+  return check_launch("decode_kernel");
+}
+
+int num_sms() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return -1;
+  return n;
+}
+
+}  // namespace
+
+// =================================================================== C ABI
+extern "C" {
+
+const char* b2a_last_error(void) { return g_err.c_str(); }
+
+int b2a_abi_version(void) { return B2A_ABI_VERSION; }
+
+int b2a_device_error(void* stream, int* code_out) {
+  if (!code_out) return fail(B2A_ERR_INVALID, "code_out is NULL");
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  int code = 0, zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(&code, b2a::g_watchdog, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaMemcpyToSymbolAsync(b2a::g_watchdog, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "device_error: %s", cudaGetErrorString(e));
+  *code_out = code;
+  return ok();
+}
+
+// ------------------------------------------------------------------ store
+int b2a_rope_store(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride, const void* v,
+                   int64_t v_row_stride, const int32_t* positions, const int32_t* out_loc, void* k_pool,
+                   void* v_pool, int64_t num_slots, const float* inv_freq, float rope_scale, int rot_dim, int T,
+                   int Hq, int Hkv, int D, int dtype, void* stream) {
+  if (T < 0) return fail(B2A_ERR_INVALID, "T must be >= 0");
+  if (T == 0) return ok();
+  if (Hq < 0 || Hkv <= 0 || D <= 0) return fail(B2A_ERR_INVALID, "bad head shape");
+  if (rot_dim < 0 || rot_dim > D || (rot_dim & 1)) return fail(B2A_ERR_INVALID, "rot_dim %d invalid for D %d", rot_dim, D);
+  const bool rotate = rot_dim > 0;
+  const bool store = k_pool != nullptr || v_pool != nullptr;
+  if (store && (!k_pool || !v_pool || !out_loc || !v)) return fail(B2A_ERR_INVALID, "store needs k_pool, v_pool, v, out_loc");
+  if (store && num_slots <= 0) return fail(B2A_ERR_INVALID, "num_slots must be > 0");
+  if (rotate && (!positions || !inv_freq)) return fail(B2A_ERR_INVALID, "rope needs positions and inv_freq");
+  if (!k || (rotate && Hq > 0 && !q)) return fail(B2A_ERR_INVALID, "q/k pointers are NULL");
+  if (q_row_stride < (int64_t)Hq * D || k_row_stride < (int64_t)Hkv * D || (store && v_row_stride < (int64_t)Hkv * D))
+    return fail(B2A_ERR_INVALID, "row strides smaller than a token row");
+  b2a::RopeStoreArgs a;
+  a.q = q;
+  a.q_stride = q_row_stride;
+  a.k = k;
+  a.k_stride = k_row_stride;
+  a.v = v;
+  a.v_stride = v_row_stride;
+  a.positions = positions;
+  a.out_loc = out_loc;
+  a.k_pool = store ? k_pool : nullptr;
+  a.v_pool = store ? v_pool : nullptr;
+  a.inv_freq = inv_freq;
+  a.rope_scale = rope_scale;
+  a.rot_dim = rot_dim;
+  a.num_slots = num_slots;
+  a.T = T;
+  a.Hq = rotate ? Hq : 0;  // q rows only matter when rotating
+  a.Hkv = Hkv;
+  a.D = D;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int64_t rows = (int64_t)T * (a.Hq + 2 * Hkv);
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many rows");
+  return with_dtype<true>(dtype, [&](auto tag) {
+    using Tt = decltype(tag);
+    b2a::rope_store_kernel<Tt><<<(unsigned)blocks, 256, 0, st>>>(a);
+    return check_launch("rope_store_kernel");
+  });
+}
+
+int b2a_store_kv(const void* k, int64_t k_row_stride, const void* v, int64_t v_row_stride, const int32_t* out_loc,
+                 void* k_pool, void* v_pool, int64_t num_slots, int T, int Hkv, int D, int dtype, void* stream) {
+  if (!k_pool || !v_pool) return fail(B2A_ERR_INVALID, "k_pool/v_pool are NULL");
+  return b2a_rope_store(nullptr, 0, const_cast<void*>(k), k_row_stride, v, v_row_stride, nullptr, out_loc, k_pool,
+                        v_pool, num_slots, nullptr, 1.0f, 0, T, 0, Hkv, D, dtype, stream);
+}
+
+// ------------------------------------------------------------------ decode
+int b2a_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B, int page_size, int num_ctas,
+                    int32_t* cta_indptr, int32_t* segs, int seg_capacity, int32_t* merge_indptr, int* n_segs,
+                    int* n_partials) {
+  if (B < 0 || num_ctas <= 0) return fail(B2A_ERR_INVALID, "B must be >= 0 and num_ctas > 0");
+  if (!kv_indptr || !cta_indptr || !segs || !merge_indptr || !n_segs || !n_partials)
+    return fail(B2A_ERR_INVALID, "NULL plan argument");
+  if (ilog2_exact(page_size) < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
+  if (kv_indptr[0] != 0) return fail(B2A_ERR_INVALID, "kv_indptr[0] must be 0");
+  for (int b = 0; b < B; ++b) {
+    if (kv_indptr[b + 1] < kv_indptr[b]) return fail(B2A_ERR_INVALID, "kv_indptr not monotonic at %d", b);
+    if (kv_last_page_len && kv_indptr[b + 1] > kv_indptr[b] &&
+        (kv_last_page_len[b] < 1 || kv_last_page_len[b] > page_size))
+      return fail(B2A_ERR_INVALID, "kv_last_page_len[%d]=%d out of [1, %d]", b, kv_last_page_len[b], page_size);
+  }
+  const int64_t total = kv_indptr[B];
+  const int64_t per = std::max<int64_t>(1, (total + num_ctas - 1) / num_ctas);
+  int ns = 0, np = 0;
+  std::fill(cta_indptr, cta_indptr + num_ctas + 1, 0);
+  std::vector<int> seg_cta;
+  seg_cta.reserve(B + num_ctas);
+  merge_indptr[0] = 0;
+  for (int b = 0; b < B; ++b) {
+    const int64_t p0 = kv_indptr[b], p1 = kv_indptr[b + 1];
+    const int last = (p1 > p0) ? (kv_last_page_len ? kv_last_page_len[b] : page_size) : 0;
+    // pieces: page ranges cut at multiples of `per`
+    int pieces = 0;
+    int64_t s = p0;
+    do {
+      const int64_t cta = std::min<int64_t>(s / per, num_ctas - 1);
+      const int64_t cut = (cta == num_ctas - 1) ? p1 : std::min<int64_t>(p1, (cta + 1) * per);
+      ++pieces;
+      s = cut;
+    } while (s < p1);
+    const bool split = pieces > 1;
+    s = p0;
+    do {
+      const int64_t cta = std::min<int64_t>(s / per, num_ctas - 1);
+      const int64_t cut = (cta == num_ctas - 1) ? p1 : std::min<int64_t>(p1, (cta + 1) * per);
+      if (ns >= seg_capacity) return fail(B2A_ERR_WORKSPACE, "seg_capacity %d too small", seg_capacity);
+      int64_t ntok = (cut - s) * page_size;
+      if (cut == p1 && p1 > p0) ntok -= (page_size - last);
+      segs[4 * ns + 0] = b;
+      segs[4 * ns + 1] = (int32_t)s;
+      segs[4 * ns + 2] = (int32_t)ntok;
+      segs[4 * ns + 3] = split ? np++ : -1;
+      seg_cta.push_back((int)cta);
+      ++ns;
+      s = cut;
+    } while (s < p1);
+    merge_indptr[b + 1] = np;
+  }
+  // Segments were emitted in page order, so their CTA ids are non-decreasing.
+  for (int i = 0; i < ns; ++i) cta_indptr[seg_cta[i] + 1]++;
+  for (int c = 0; c < num_ctas; ++c) cta_indptr[c + 1] += cta_indptr[c];
+  *n_segs = ns;
+  *n_partials = np;
+  return ok();
+}
+
+int b2a_decode_num_ctas(int Hq, int Hkv, int D, int dtype, int* num_ctas) {
+  if (!num_ctas) return fail(B2A_ERR_INVALID, "num_ctas is NULL");
+  if (int rc = check_heads(Hq, Hkv, D)) return rc;
+  const size_t es = dtype_size(dtype);
+  if (es == 0 || dtype == B2A_DTYPE_F16) return fail(B2A_ERR_UNSUPPORTED, "decode dtype %d", dtype);
+  DecodeCfg c;
+  if (int rc = decode_config(Hq, Hkv, D, es, c)) return rc;
+  const int sms = num_sms();
+  if (sms <= 0) return fail(B2A_ERR_CUDA, "no CUDA device");
+  // One CTA per SM: the kernel is sized to own an SM's shared memory.
+  const int per_sm = std::max<int>(1, (int)(kSmemLimit / (c.smem + 1024)));
+  *num_ctas = sms * per_sm;
+  return ok();
+}
+
+size_t b2a_decode_workspace_bytes(int n_partials, int Hq, int D) {
+  if (n_partials <= 0) return 0;
+  const size_t acc = (size_t)n_partials * Hq * D * sizeof(float);
+  const size_t ml = (size_t)n_partials * Hq * 2 * sizeof(float);
+  return ((acc + 255) & ~(size_t)255) + ml;
+}
+
+static int decode_common(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                         const int32_t* kv_indices,
+                         const int32_t* kv_indptr, int page_size, const int32_t* cta_indptr, const int32_t* segs,
+                         int grid, const int32_t* merge_indptr, int n_partials, int B, int Hq, int Hkv, int D,
+                         float scale, void* workspace, size_t workspace_bytes, void* out, int dtype, void* stream) {
+  if (B < 0) return fail(B2A_ERR_INVALID, "B must be >= 0");
+  if (B == 0) return ok();
+  if (int rc = check_heads(Hq, Hkv, D)) return rc;
+  if (!q || !k_pool || !v_pool || !kv_indices || !out) return fail(B2A_ERR_INVALID, "NULL tensor pointer");
+  if (num_slots <= 0) return fail(B2A_ERR_INVALID, "num_slots must be > 0");
+  if (!aligned(q, 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(out, 16))
+    return fail(B2A_ERR_INVALID, "q/k_pool/v_pool/out must be 16-byte aligned");
+  const int plog = ilog2_exact(page_size);
+  if (plog < 0 || page_size > 4096) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two <= 4096", page_size);
+  const size_t es = dtype_size(dtype);
+  if (es == 0 || dtype == B2A_DTYPE_F16) return fail(B2A_ERR_UNSUPPORTED, "decode dtype %d", dtype);
+  DecodeCfg c;
+  if (int rc = decode_config(Hq, Hkv, D, es, c)) return rc;
+  const size_t need = b2a_decode_workspace_bytes(n_partials, Hq, D);
+  if (n_partials > 0 && (!workspace || workspace_bytes < need || !merge_indptr))
+    return fail(B2A_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
+  if (workspace && !aligned(workspace, 256)) return fail(B2A_ERR_INVALID, "workspace must be 256-byte aligned");
+  b2a::DecodeArgs a;
+  a.q = q;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.kv_indices = kv_indices;
+  a.num_slots = num_slots;
+  a.kv_indptr = kv_indptr;
+  a.cta_indptr = cta_indptr;
+  a.segs = segs;
+  a.ws_acc = reinterpret_cast<float*>(workspace);
+  a.ws_ml = n_partials > 0 ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
+                                                      (((size_t)n_partials * Hq * D * 4 + 255) & ~(size_t)255))
+                           : nullptr;
+  a.out = out;
+  a.page_log2 = plog;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.qscale = scale * b2a::kLog2e;
+  a.TS = c.TS;
+  a.NSTAGE = c.NSTAGE;
+  a.WPH = c.WPH;
+  a.NCW = c.NCW;
+  a.row_bytes = c.row_bytes;
+  a.stage_bytes = c.stage_bytes;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int G = Hq / Hkv;
+  int rc = with_dtype<false>(dtype, [&](auto tag) {
+    using Tt = decltype(tag);
+    return with_d(D, [&](auto dc) {
+      constexpr int Dc = decltype(dc)::value;
+      return with_g<Dc>(G, [&](auto gc) {
+        constexpr int Gc = decltype(gc)::value;
+        if (int r = decode_launch<Tt, Dc, Gc>(a, c, grid, st)) return r;
+        if (n_partials > 0) {
+          const int blocks = (B * Hq + 3) / 4;
+          b2a::decode_merge_kernel<Tt, Dc><<<blocks, 128, 0, st>>>(a.ws_acc, a.ws_ml, merge_indptr, out, B, Hq);
+          return check_launch("decode_merge_kernel");
+        }
+        return ok();
+      });
+    });
+  });
+  return rc;
+}
+
+int b2a_paged_decode(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                     const int32_t* kv_indptr, const int32_t* kv_indices, int B, int Hq, int Hkv, int D, float scale,
+                     void* out, int dtype, void* stream) {
+  if (!kv_indptr) return fail(B2A_ERR_INVALID, "kv_indptr is NULL");
+  return decode_common(q, k_pool, v_pool, num_slots, kv_indices, kv_indptr, 1, nullptr, nullptr, B, nullptr, 0, B, Hq, Hkv,
+                       D, scale, nullptr, 0, out, dtype, stream);
+}
+
+int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots, const int32_t* kv_indices,
+               int page_size,
+               const int32_t* cta_indptr, const int32_t* segs, int num_ctas, const int32_t* merge_indptr,
+               int n_partials, int B, int Hq, int Hkv, int D, float scale, void* workspace, size_t workspace_bytes,
+               void* out, int dtype, void* stream) {
+  if (!cta_indptr || !segs || num_ctas <= 0) return fail(B2A_ERR_INVALID, "decode plan missing (cta_indptr/segs)");
+  if (!aligned(segs, 16)) return fail(B2A_ERR_INVALID, "segs must be 16-byte aligned (read as int4)");
+  return decode_common(q, k_pool, v_pool, num_slots, kv_indices, nullptr, page_size, cta_indptr, segs, num_ctas, merge_indptr,
+                       n_partials, B, Hq, Hkv, D, scale, workspace, workspace_bytes, out, dtype, stream);
+}
+
+// ------------------------------------------------------------------ extend
+int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int* tile_q) {
+  if (!tile_q) return fail(B2A_ERR_INVALID, "tile_q is NULL");
+  if (int rc = check_heads(Hq, Hkv, D)) return rc;
+  const int G = Hq / Hkv;
+  if (b2a::extend_tc_supported(Hq, Hkv, D, dtype)) {
+    *tile_q = b2a::kTcRows / G;
+  } else {
+    if (G > b2a::kSimtRows) return fail(B2A_ERR_UNSUPPORTED, "GQA group %d too large", G);
+    *tile_q = b2a::kSimtRows / G;
+  }
+  return ok();
+}
+
+int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,
+                    int page_size, int tile_q, int32_t* work, int work_capacity, int* n_work) {
+  if (!qo_indptr || !kv_indptr || !work || !n_work) return fail(B2A_ERR_INVALID, "NULL plan argument");
+  if (B < 0 || tile_q <= 0) return fail(B2A_ERR_INVALID, "B must be >= 0, tile_q > 0");
+  if (ilog2_exact(page_size) < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
+  struct Item {
+    int r, tb, nq;
+    int64_t cost;
+  };
+  std::vector<Item> items;
+  for (int r = 0; r < B; ++r) {
+    const int Lq = qo_indptr[r + 1] - qo_indptr[r];
+    const int np = kv_indptr[r + 1] - kv_indptr[r];
+    if (Lq < 0 || np < 0) return fail(B2A_ERR_INVALID, "indptr not monotonic at request %d", r);
+    const int last = np > 0 ? (kv_last_page_len ? kv_last_page_len[r] : page_size) : 0;
+    if (np > 0 && (last < 1 || last > page_size))
+      return fail(B2A_ERR_INVALID, "kv_last_page_len[%d]=%d out of [1, %d]", r, last, page_size);
+    const int64_t Lkv = np > 0 ? (int64_t)(np - 1) * page_size + last : 0;
+    if (Lkv < Lq) return fail(B2A_ERR_INVALID, "request %d: kv length %lld < query length %d", r, (long long)Lkv, Lq);
+    const int64_t prefix = Lkv - Lq;
+    for (int tb = 0; tb < Lq; tb += tile_q) {
+      const int nq = std::min(tile_q, Lq - tb);
+      items.push_back({r, tb, nq, (int64_t)nq * (prefix + tb + nq)});
+    }
+  }
+  if ((int)items.size() > work_capacity) return fail(B2A_ERR_WORKSPACE, "work_capacity %d < %zu tiles", work_capacity, items.size());
+  std::stable_sort(items.begin(), items.end(), [](const Item& x, const Item& y) { return x.cost > y.cost; });
+  for (size_t i = 0; i < items.size(); ++i) {
+    work[4 * i + 0] = items[i].r;
+    work[4 * i + 1] = items[i].tb;
+    work[4 * i + 2] = items[i].nq;
+    work[4 * i + 3] = 0;
+  }
+  *n_work = (int)items.size();
+  return ok();
+}
+
+int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots, const int32_t* qo_indptr,
+               const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* kv_last_page_len, int page_size,
+               const int32_t* work, int n_work, int T, int B, int Hq, int Hkv, int D, float scale, void* out,
+               int dtype, void* stream) {
+  if (n_work < 0 || B < 0 || T < 0) return fail(B2A_ERR_INVALID, "negative size");
+  if (n_work == 0) return ok();
+  if (int rc = check_heads(Hq, Hkv, D)) return rc;
+  if (!q || !k_pool || !v_pool || !qo_indptr || !kv_indptr || !kv_indices || !work || !out)
+    return fail(B2A_ERR_INVALID, "NULL pointer argument");
+  if (!aligned(work, 16)) return fail(B2A_ERR_INVALID, "work must be 16-byte aligned (read as int4)");
+  if (!aligned(q, 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(out, 16))
+    return fail(B2A_ERR_INVALID, "q/k_pool/v_pool/out must be 16-byte aligned");
+  const int plog = ilog2_exact(page_size);
+  if (plog < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
+  if (num_slots <= 0) return fail(B2A_ERR_INVALID, "num_slots must be > 0");
+  if (dtype == B2A_DTYPE_F16 || dtype_size(dtype) == 0) return fail(B2A_ERR_UNSUPPORTED, "extend dtype %d", dtype);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const int G = Hq / Hkv;
+  if (b2a::extend_tc_supported(Hq, Hkv, D, dtype)) {
+    return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
+                                 plog, work, n_work, T, Hq, Hkv, scale, out, st, g_err);
+  }
+  if (G > b2a::kSimtRows) return fail(B2A_ERR_UNSUPPORTED, "GQA group %d too large", G);
+  b2a::ExtendArgs a;
+  a.q = q;
+  a.k_pool = k_pool;
+  a.v_pool = v_pool;
+  a.qo_indptr = qo_indptr;
+  a.kv_indptr = kv_indptr;
+  a.kv_indices = kv_indices;
+  a.kv_last_page_len = kv_last_page_len;
+  a.work = work;
+  a.out = out;
+  a.num_slots = num_slots;
+  a.page_log2 = plog;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.qscale = scale * b2a::kLog2e;
+  return with_dtype<false>(dtype, [&](auto tag) {
+    using Tt = decltype(tag);
+    return with_d(D, [&](auto dc) {
+      constexpr int Dc = decltype(dc)::value;
+      return with_g<Dc>(G, [&](auto gc) {
+        constexpr int Gc = decltype(gc)::value;
+        auto kern = b2a::extend_simt_kernel<Tt, Dc, Gc>;
+        const size_t smem = b2a::extend_simt_smem(Dc);
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "extend: smem attribute: %s", cudaGetErrorString(e));
+        kern<<<dim3(n_work, Hkv), b2a::kSimtThreads, smem, st>>>(a);
+        return check_launch("extend_simt_kernel");
+      });
+    });
+  });
+}
+
+}  // extern "C"

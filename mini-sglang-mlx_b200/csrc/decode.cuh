@@ -1,0 +1,444 @@
+// Paged decode attention (one query row per request) for sm_100a.
+//
+// Reference: python/minisgl_mlx/attention/metal.py:35-131 (Metal kernel: one
+// threadgroup per (request, kv head), online softmax, fp32 accumulation) and
+// attention/naive.py:50-60 (gather + masked SDPA, same values).
+//
+// B200 design (not a translation of the Metal kernel):
+//   * The pool row of one slot holds all Hkv heads ([Hkv, D], 2 KB for
+//     8x128 bf16), and a page is page_size consecutive rows. A CTA therefore
+//     works on ALL kv heads of a request at once and moves whole page runs
+//     with single cp.async.bulk (TMA) copies into a NSTAGE-deep shared-memory
+//     ring, completion tracked by mbarriers (one producer warp).
+//   * Grid = persistent CTAs, each owning a contiguous, equal share of the
+//     concatenated page stream of the batch (host plan). A request cut by a
+//     share boundary produces partial (m, l, acc) rows that a merge kernel
+//     combines; requests inside a share are written directly.
+//   * Consumer warp w serves kv head w / WPH. Lane = D/32 features. The G
+//     query heads of the group share every K/V row read. Per group of 32/G
+//     tokens the G*32/G = 32 partial dot products are reduced with a
+//     transpose-butterfly (31 shuffles for 32 sums), leaving lane l with the
+//     score of (token l/G, head l%G); softmax statistics are per lane, the
+//     probabilities go through a 32-float smem slot to the PV loop.
+//   * Scores are kept in the log2 domain (q pre-scaled by scale*log2 e).
+#pragma once
+#include <type_traits>
+
+#include "common.cuh"
+
+namespace b2a {
+
+struct DecodeArgs {
+  const void* q;
+  const void* k_pool;
+  const void* v_pool;
+  const int32_t* kv_indices;  // page ids
+  const int32_t* kv_indptr;   // direct mode: token CSR (page_size 1)
+  const int32_t* cta_indptr;  // plan mode: CSR over segs; NULL = direct mode
+  const int32_t* segs;        // int4 {request, first page idx, n_tokens, out_slot}
+  float* ws_acc;              // [n_partials, Hq, D]
+  float* ws_ml;               // [n_partials, Hq, 2]
+  void* out;                  // [B, Hq, D]
+  int64_t num_slots;
+  int page_log2;
+  int Hq, Hkv;
+  float qscale;  // softmax scale * log2(e)
+  int TS;        // tokens per stage
+  int NSTAGE;
+  int WPH;  // consumer warps per kv head
+  int NCW;  // consumer warps
+  uint32_t row_bytes;
+  uint32_t stage_bytes;  // bytes of ONE of K/V in a stage (TS * row_bytes)
+};
+
+struct DecodeSmem {
+  // byte offsets inside the dynamic shared memory block
+  uint32_t bars, pbuf, cbuf, abort_flag, total;
+};
+
+__host__ __device__ inline DecodeSmem decode_smem_layout(int NSTAGE, uint32_t stage_bytes, int NCW, int WPH,
+                                                         int G, int D) {
+  DecodeSmem L;
+  uint32_t off = (uint32_t)NSTAGE * 2u * stage_bytes;
+  off = (off + 127u) & ~127u;
+  L.bars = off;
+  off += (uint32_t)NSTAGE * 2u * 8u;
+  off = (off + 15u) & ~15u;
+  L.pbuf = off;
+  off += (uint32_t)NCW * 32u * 4u;
+  L.cbuf = off;
+  if (WPH > 1) off += (uint32_t)NCW * (uint32_t)G * (uint32_t)(D + 2) * 4u;
+  L.abort_flag = off;
+  off += 16;
+  L.total = off;
+  return L;
+}
+
+__device__ __forceinline__ void decode_get_seg(const DecodeArgs& a, int idx, int& b, int& page_begin, int& ntok,
+                                               int& slot) {
+  if (a.cta_indptr != nullptr) {
+    const int4 s = reinterpret_cast<const int4*>(a.segs)[idx];
+    b = s.x;
+    page_begin = s.y;
+    ntok = s.z;
+    slot = s.w;
+  } else {
+    b = blockIdx.x;
+    page_begin = a.kv_indptr[b];
+    ntok = a.kv_indptr[b + 1] - page_begin;
+    slot = -1;
+  }
+}
+
+template <int G>
+__device__ __forceinline__ void load_p(const float* pb, int i, float (&pg)[G]) {
+  if constexpr (G == 1) {
+    pg[0] = pb[i];
+  } else if constexpr (G == 2) {
+    const float2 t = reinterpret_cast<const float2*>(pb)[i];
+    pg[0] = t.x;
+    pg[1] = t.y;
+  } else {
+#pragma unroll
+    for (int j = 0; j < G / 4; ++j) {
+      const float4 t = reinterpret_cast<const float4*>(pb + i * G)[j];
+      pg[4 * j + 0] = t.x;
+      pg[4 * j + 1] = t.y;
+      pg[4 * j + 2] = t.z;
+      pg[4 * j + 3] = t.w;
+    }
+  }
+}
+
+// One group of TG = 32/G tokens of the current stage for one kv head.
+template <typename T, int D, int G>
+__device__ __forceinline__ void decode_group(const T* __restrict__ Ks, const T* __restrict__ Vs, int t0,
+                                             int nvalid, int h, int Hkv, int lane,
+                                             const float (&qv)[G][D / 32], float (&acc)[G][D / 32],
+                                             float& m_mine, float& l_mine, float* pb) {
+  constexpr int EPT = D / 32;
+  constexpr int TG = 32 / G;
+  constexpr unsigned FULL = 0xffffffffu;
+  float v[32];
+#pragma unroll
+  for (int i = 0; i < TG; ++i) {
+    if (i < nvalid) {
+      float kf[EPT];
+      load_vec<T, EPT>(Ks + ((size_t)(t0 + i) * Hkv + h) * D + lane * EPT, kf);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+        float s = 0.f;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) s = fmaf(qv[g][e], kf[e], s);
+        v[i * G + g] = s;
+      }
+    } else {
+#pragma unroll
+      for (int g = 0; g < G; ++g) v[i * G + g] = 0.f;
+    }
+  }
+  // Transpose-butterfly: after the step with offset `off`, lanes with that bit
+  // set keep the upper half of the remaining values. Lane l ends holding the
+  // full sum of value l.
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < off; ++j) {
+      const float lo = v[j], hi = v[j + off];
+      const float send = upper ? lo : hi;
+      const float keep = upper ? hi : lo;
+      v[j] = keep + __shfl_xor_sync(FULL, send, off);
+    }
+  }
+  const int my_tok = lane / G;
+  const float s = (my_tok < nvalid) ? v[0] : kNegInf;
+  float mt = s;
+#pragma unroll
+  for (int off = G; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(FULL, mt, off));
+  const float m_new = fmaxf(m_mine, mt);
+  const float alpha = (m_mine == m_new) ? 1.f : exp2f(m_mine - m_new);
+  const float p = (s == kNegInf) ? 0.f : exp2f(s - m_new);
+  l_mine = l_mine * alpha + p;
+  m_mine = m_new;
+  pb[lane] = p;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float ag = __shfl_sync(FULL, alpha, g);
+    if (ag != 1.f) {
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) acc[g][e] *= ag;
+    }
+  }
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < TG; ++i) {
+    if (i < nvalid) {
+      float vf[EPT];
+      load_vec<T, EPT>(Vs + ((size_t)(t0 + i) * Hkv + h) * D + lane * EPT, vf);
+      float pg[G];
+      load_p<G>(pb, i, pg);
+#pragma unroll
+      for (int g = 0; g < G; ++g)
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) acc[g][e] = fmaf(pg[g], vf[e], acc[g][e]);
+    }
+  }
+  __syncwarp();
+}
+
+template <typename T, int D, int G>
+__global__ void __launch_bounds__(288, 1) decode_kernel(const DecodeArgs a) {
+  constexpr int EPT = D / 32;
+  constexpr unsigned FULL = 0xffffffffu;
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int G_ = G;
+  const DecodeSmem L = decode_smem_layout(a.NSTAGE, a.stage_bytes, a.NCW, a.WPH, G_, D);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bars);
+  uint64_t* empty = full + a.NSTAGE;
+  volatile int* s_abort = reinterpret_cast<volatile int*>(smem + L.abort_flag);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < a.NSTAGE; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], a.NCW);
+    }
+    *s_abort = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+
+  int seg0, seg1;
+  if (a.cta_indptr != nullptr) {
+    seg0 = a.cta_indptr[blockIdx.x];
+    seg1 = a.cta_indptr[blockIdx.x + 1];
+  } else {
+    seg0 = 0;
+    seg1 = 1;
+  }
+  const int P = 1 << a.page_log2;
+  const int TS = a.TS;
+
+  if (warp == a.NCW) {
+    // ------------------------------------------------------------ producer
+    const uint64_t pol = l2_evict_first_policy();
+    const uint8_t* kp = reinterpret_cast<const uint8_t*>(a.k_pool);
+    const uint8_t* vp = reinterpret_cast<const uint8_t*>(a.v_pool);
+    const size_t rowB = a.row_bytes;
+    int ctr = 0;
+    bool ok = true;
+    for (int si = seg0; si < seg1 && ok; ++si) {
+      int b, pbeg, ntok, slot;
+      decode_get_seg(a, si, b, pbeg, ntok, slot);
+      for (int tok = 0; tok < ntok; tok += TS) {
+        if (!__all_sync(FULL, *s_abort == 0)) {
+          ok = false;
+          break;
+        }
+        const int nt = min(TS, ntok - tok);
+        const int st = ctr % a.NSTAGE;
+        const uint32_t ph = (uint32_t)(ctr / a.NSTAGE) & 1u;
+        const bool got = __all_sync(FULL, mbar_wait(&empty[st], ph ^ 1u, kWdDecodeEmpty));
+        if (!got) {
+          *s_abort = 1;
+          ok = false;
+          break;
+        }
+        uint8_t* kdst = smem + (size_t)st * 2u * a.stage_bytes;
+        uint8_t* vdst = kdst + a.stage_bytes;
+        // A stage is either a run inside one page (P >= TS) or whole pages
+        // (P < TS, stages start on page boundaries); lane j owns copy j.
+        const bool one_run = P >= TS;
+        const int ncopies = one_run ? 1 : ((nt + P - 1) >> a.page_log2);
+        int64_t src_slot[2] = {0, 0};
+        int rows_of[2] = {0, 0};
+        bool in_range = true;
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+          const int j = lane + 32 * u;
+          if (j < ncopies) {
+            const int64_t page = a.kv_indices[pbeg + (tok >> a.page_log2) + j];
+            src_slot[u] = one_run ? page * P + (tok & (P - 1)) : page * P;
+            rows_of[u] = one_run ? nt : min(P, nt - j * P);
+            in_range = in_range && page >= 0 && src_slot[u] + rows_of[u] <= a.num_slots;
+          }
+        }
+        // Bad page ids never reach the copy engine: record the error, skip the
+        // copies of this stage and let the consumers run on stale data.
+        const bool all_ok = __all_sync(FULL, in_range);
+        if (!all_ok && lane == 0) watchdog_set(kWdBadSlot);
+        if (lane == 0) {
+          if (all_ok) mbar_arrive_expect_tx(&full[st], (uint32_t)(2u * (uint32_t)nt * a.row_bytes));
+          else mbar_arrive(&full[st]);
+        }
+        __syncwarp();
+        if (all_ok) {
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int j = lane + 32 * u;
+            if (j < ncopies) {
+              const uint32_t bytes = (uint32_t)rows_of[u] * a.row_bytes;
+              const size_t doff = (size_t)j * P * rowB;
+              bulk_g2s(kdst + doff, kp + src_slot[u] * rowB, bytes, &full[st], pol);
+              bulk_g2s(vdst + doff, vp + src_slot[u] * rowB, bytes, &full[st], pol);
+            }
+          }
+        }
+        __syncwarp();
+        ++ctr;
+      }
+    }
+    // Never leave while our own bulk copies may still be landing.
+    const int first = ctr > a.NSTAGE ? ctr - a.NSTAGE : 0;
+    for (int i = first; i < ctr; ++i)
+      mbar_wait(&full[i % a.NSTAGE], (uint32_t)(i / a.NSTAGE) & 1u, kWdDecodeDrain);
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  const int h = warp / a.WPH;
+  const int sub = warp - h * a.WPH;
+  float* pb = reinterpret_cast<float*>(smem + L.pbuf) + warp * 32;
+  float* cbuf = reinterpret_cast<float*>(smem + L.cbuf);
+  const T* qbase = reinterpret_cast<const T*>(a.q);
+  int ctr = 0;
+  for (int si = seg0; si < seg1; ++si) {
+    int b, pbeg, ntok, slot;
+    decode_get_seg(a, si, b, pbeg, ntok, slot);
+    float qv[G][EPT], acc[G][EPT];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      load_vec<T, EPT>(qbase + ((size_t)b * a.Hq + h * G + g) * D + lane * EPT, qv[g]);
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) {
+        qv[g][e] *= a.qscale;
+        acc[g][e] = 0.f;
+      }
+    }
+    float m_mine = kNegInf, l_mine = 0.f;
+    for (int tok = 0; tok < ntok; tok += TS) {
+      const int nt = min(TS, ntok - tok);
+      const int st = ctr % a.NSTAGE;
+      const uint32_t ph = (uint32_t)(ctr / a.NSTAGE) & 1u;
+      bool ok = __all_sync(FULL, *s_abort == 0);
+      if (ok) ok = __all_sync(FULL, mbar_wait(&full[st], ph, kWdDecodeFull));
+      if (!ok) *s_abort = 1;
+      if (ok) {
+        const T* Ks = reinterpret_cast<const T*>(smem + (size_t)st * 2u * a.stage_bytes);
+        const T* Vs = reinterpret_cast<const T*>(smem + (size_t)st * 2u * a.stage_bytes + a.stage_bytes);
+        for (int t0 = sub * (32 / G); t0 < nt; t0 += a.WPH * (32 / G)) {
+          decode_group<T, D, G>(Ks, Vs, t0, min(32 / G, nt - t0), h, a.Hkv, lane, qv, acc, m_mine, l_mine, pb);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[st]);
+      ++ctr;
+    }
+    // ---- finalize this segment
+    float l_red = l_mine;
+#pragma unroll
+    for (int off = G; off < 32; off <<= 1) l_red += __shfl_xor_sync(FULL, l_red, off);
+    float mg[G], lg[G];
+#pragma unroll
+    for (int g = 0; g < G; ++g) {
+      mg[g] = __shfl_sync(FULL, m_mine, g);
+      lg[g] = __shfl_sync(FULL, l_red, g);
+    }
+    if (a.WPH > 1) {
+      float* mine = cbuf + (size_t)warp * G * (D + 2);
+#pragma unroll
+      for (int g = 0; g < G; ++g) {
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) mine[g * (D + 2) + lane * EPT + e] = acc[g][e];
+        if (lane == 0) {
+          mine[g * (D + 2) + D] = mg[g];
+          mine[g * (D + 2) + D + 1] = lg[g];
+        }
+      }
+      named_bar_sync(1, a.NCW * 32);
+      if (sub == 0) {
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          float M = kNegInf;
+          for (int s2 = 0; s2 < a.WPH; ++s2) M = fmaxf(M, cbuf[(size_t)(warp + s2) * G * (D + 2) + g * (D + 2) + D]);
+          float Lsum = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPT; ++e) acc[g][e] = 0.f;
+          for (int s2 = 0; s2 < a.WPH; ++s2) {
+            const float* o = cbuf + (size_t)(warp + s2) * G * (D + 2) + g * (D + 2);
+            const float w = (o[D] == kNegInf) ? 0.f : exp2f(o[D] - M);
+            Lsum += o[D + 1] * w;
+#pragma unroll
+            for (int e = 0; e < EPT; ++e) acc[g][e] = fmaf(w, o[lane * EPT + e], acc[g][e]);
+          }
+          mg[g] = M;
+          lg[g] = Lsum;
+        }
+      }
+    }
+    if (sub == 0) {
+      if (slot < 0) {
+        T* o = reinterpret_cast<T*>(a.out) + ((size_t)b * a.Hq + h * G) * D + lane * EPT;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          const float inv = lg[g] > 0.f ? 1.f / lg[g] : 0.f;
+          float r[EPT];
+#pragma unroll
+          for (int e = 0; e < EPT; ++e) r[e] = acc[g][e] * inv;
+          store_vec<T, EPT>(o + (size_t)g * D, r);
+        }
+      } else {
+        float* o = a.ws_acc + ((size_t)slot * a.Hq + h * G) * D + lane * EPT;
+#pragma unroll
+        for (int g = 0; g < G; ++g) {
+          store_vec<float, EPT>(o + (size_t)g * D, acc[g]);
+          if (lane == 0) {
+            a.ws_ml[((size_t)slot * a.Hq + h * G + g) * 2 + 0] = mg[g];
+            a.ws_ml[((size_t)slot * a.Hq + h * G + g) * 2 + 1] = lg[g];
+          }
+        }
+      }
+    }
+    if (a.WPH > 1) named_bar_sync(1, a.NCW * 32);
+  }
+}
+
+// Combine the partial rows of requests that were cut across CTAs.
+template <typename T, int D>
+__global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restrict__ ws_acc,
+                                                           const float* __restrict__ ws_ml,
+                                                           const int32_t* __restrict__ merge_indptr, void* out,
+                                                           int B, int Hq) {
+  constexpr int EPT = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int idx = blockIdx.x * 4 + (threadIdx.x >> 5);
+  if (idx >= B * Hq) return;
+  const int b = idx / Hq;
+  const int qh = idx - b * Hq;
+  const int p0 = merge_indptr[b], p1 = merge_indptr[b + 1];
+  if (p1 <= p0) return;
+  float M = kNegInf;
+  for (int p = p0; p < p1; ++p) M = fmaxf(M, ws_ml[((size_t)p * Hq + qh) * 2]);
+  float Lsum = 0.f, acc[EPT];
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) acc[e] = 0.f;
+  for (int p = p0; p < p1; ++p) {
+    const float m = ws_ml[((size_t)p * Hq + qh) * 2];
+    const float l = ws_ml[((size_t)p * Hq + qh) * 2 + 1];
+    const float w = (m == kNegInf) ? 0.f : exp2f(m - M);
+    Lsum += l * w;
+    float o[EPT];
+    load_vec<float, EPT>(ws_acc + ((size_t)p * Hq + qh) * D + lane * EPT, o);
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) acc[e] = fmaf(w, o[e], acc[e]);
+  }
+  const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+  for (int e = 0; e < EPT; ++e) acc[e] *= inv;
+  store_vec<T, EPT>(reinterpret_cast<T*>(out) + ((size_t)b * Hq + qh) * D + lane * EPT, acc);
+}
+
+}  // namespace b2a

@@ -1,0 +1,194 @@
+"""The B200 attention backend (``--attn b200``).
+
+Drop-in for the reference's backends (python/minisgl_mlx/attention/
+{base,naive,metal}.py): same constructor ``(config, kv_cache, page_table)``,
+same ``prepare_metadata`` / ``forward`` / ``prepare_decode`` /
+``forward_decode`` contract, computed by the CUDA kernels of libb200attn.so:
+
+* decode  -> ``b2a_decode``: persistent split-KV paged decode + merge
+  (replaces metal.py:112-162 and naive.py:36-60)
+* prefill -> ``b2a_extend``: ragged causal extend over the paged prefix
+  (replaces base.py:107-142)
+
+There is no CPU or library fallback: without the CUDA library or a GPU the
+backend refuses to construct.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List
+
+import numpy as np
+import torch
+
+from .. import _native as nat
+from ..core import get_global_ctx
+from ..kvcache.pool import current_stream_ptr, dtype_code
+from .base import CHECK_METADATA, BaseAttnBackend, PinnedStager, paged_kv_indices
+
+
+@dataclass
+class B200DecodeMetadata:
+    kv_indptr: torch.Tensor  # int32 [B+1] page CSR (device)
+    kv_indices: torch.Tensor  # int32 [sum pages] page ids (device)
+    kv_last_page_len: torch.Tensor  # int32 [B] (device)
+    cta_indptr: torch.Tensor  # int32 [num_ctas+1] (device)
+    segs: torch.Tensor  # int32 [n_segs, 4] (device)
+    merge_indptr: torch.Tensor  # int32 [B+1] (device)
+    n_partials: int
+    num_ctas: int
+    page_size: int
+    batch_size: int
+
+
+@dataclass
+class B200PrefillMetadata:
+    last_indices: torch.Tensor  # int32 [B] (device): last token of each request in the packed batch
+    q_offsets: List[int]  # [B+1] host, as reference PrefillMetadata
+    qo_indptr: torch.Tensor  # int32 [B+1] (device)
+    kv_indptr: torch.Tensor  # int32 [B+1] page CSR (device)
+    kv_indices: torch.Tensor  # int32 page ids (device)
+    kv_last_page_len: torch.Tensor  # int32 [B] (device)
+    work: torch.Tensor  # int32 [n_work, 4] (device)
+    n_work: int
+    total_q: int
+    page_size: int
+
+
+def _page_size() -> int:
+    try:
+        return int(get_global_ctx().page_size)
+    except AssertionError:
+        return 1
+
+
+class B200AttnBackend(BaseAttnBackend):
+    def __init__(self, config, kv_cache, page_table: np.ndarray, page_size: int | None = None) -> None:
+        super().__init__(config, kv_cache, page_table)
+        if not torch.cuda.is_available():
+            raise RuntimeError("the b200 attention backend needs a CUDA device")
+        self.device = kv_cache.device
+        self.Hq = config.num_qo_heads
+        self.Hkv = config.num_kv_heads
+        self.D = config.head_dim
+        self.dtype_code = dtype_code(kv_cache.dtype)
+        self._page_size = page_size
+        self._stager = PinnedStager()
+        self._workspace = torch.empty(0, dtype=torch.uint8, device=self.device)
+        n = nat.ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            nat.call("b2a_decode_num_ctas", self.Hq, self.Hkv, self.D, self.dtype_code, nat.ctypes.byref(n))
+        self.num_ctas = n.value
+        self.tile_q = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code)
+
+    # ------------------------------------------------------------ helpers
+    @property
+    def page_size(self) -> int:
+        return self._page_size if self._page_size is not None else _page_size()
+
+    def _workspace_for(self, nbytes: int) -> torch.Tensor:
+        if self._workspace.numel() < nbytes:
+            self._workspace = torch.empty(max(nbytes, 2 * self._workspace.numel()), dtype=torch.uint8,
+                                          device=self.device)
+        return self._workspace
+
+    # ------------------------------------------------------------ decode
+    def prepare_decode(self, batch) -> B200DecodeMetadata:
+        lens = np.array([r.device_len for r in batch.reqs], dtype=np.int64)
+        rows = np.array([r.table_idx for r in batch.reqs], dtype=np.int64)
+        return self.decode_metadata_from_lens(rows, lens)
+
+    def decode_metadata_from_lens(self, rows: np.ndarray, lens: np.ndarray,
+                                  num_ctas: int | None = None) -> B200DecodeMetadata:
+        P = self.page_size
+        kv_indptr, kv_indices, lpl = paged_kv_indices(self.page_table, rows, lens, P, check=CHECK_METADATA)
+        nctas = num_ctas or self.num_ctas
+        cta_indptr, segs, merge_indptr, n_partials = nat.decode_plan(kv_indptr, lpl, P, nctas)
+        if CHECK_METADATA and kv_indices.size and int(kv_indices.max()) * P >= self.kv_cache.num_tokens:
+            raise ValueError("kv_indices point past the end of the KV pool")
+        dev = self._stager.upload([kv_indptr, kv_indices, lpl, cta_indptr, segs, merge_indptr], self.device)
+        return B200DecodeMetadata(
+            kv_indptr=dev[0], kv_indices=dev[1], kv_last_page_len=dev[2], cta_indptr=dev[3],
+            segs=dev[4].view(-1, 4), merge_indptr=dev[5], n_partials=n_partials, num_ctas=nctas,
+            page_size=P, batch_size=len(lens),
+        )
+
+    def forward_decode(self, q: torch.Tensor, layer_id: int, meta: B200DecodeMetadata) -> torch.Tensor:
+        B = meta.batch_size
+        assert q.shape == (B, self.Hq, self.D), q.shape
+        q = q.contiguous()
+        out = torch.empty_like(q)
+        ws_bytes = nat.decode_workspace_bytes(meta.n_partials, self.Hq, self.D)
+        ws = self._workspace_for(ws_bytes)
+        nat.call(
+            "b2a_decode", q.data_ptr(), self.kv_cache.k_cache(layer_id).data_ptr(),
+            self.kv_cache.v_cache(layer_id).data_ptr(), self.kv_cache.num_tokens, meta.kv_indices.data_ptr(),
+            meta.page_size,
+            meta.cta_indptr.data_ptr(), meta.segs.data_ptr(), meta.num_ctas, meta.merge_indptr.data_ptr(),
+            meta.n_partials, B, self.Hq, self.Hkv, self.D, float(self.scale), ws.data_ptr(), ws.numel(),
+            out.data_ptr(), self.dtype_code, current_stream_ptr(self.device),
+        )
+        return out
+
+    # ------------------------------------------------------------ prefill / extend
+    def _prepare_prefill(self, batch) -> B200PrefillMetadata:
+        extend = np.array([r.extend_len for r in batch.reqs], dtype=np.int64)
+        lens = np.array([r.device_len for r in batch.reqs], dtype=np.int64)
+        rows = np.array([r.table_idx for r in batch.reqs], dtype=np.int64)
+        return self.extend_metadata_from_lens(rows, lens, extend)
+
+    def extend_metadata_from_lens(self, rows: np.ndarray, lens: np.ndarray,
+                                  extend: np.ndarray) -> B200PrefillMetadata:
+        P = self.page_size
+        qo_indptr = np.zeros(len(extend) + 1, np.int32)
+        np.cumsum(extend, out=qo_indptr[1:])
+        kv_indptr, kv_indices, lpl = paged_kv_indices(self.page_table, rows, lens, P, check=CHECK_METADATA)
+        work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, self.tile_q)
+        last_indices = (qo_indptr[1:] - 1).astype(np.int32)
+        dev = self._stager.upload([last_indices, qo_indptr, kv_indptr, kv_indices, lpl, work], self.device)
+        return B200PrefillMetadata(
+            last_indices=dev[0], q_offsets=qo_indptr.tolist(), qo_indptr=dev[1], kv_indptr=dev[2],
+            kv_indices=dev[3], kv_last_page_len=dev[4], work=dev[5].view(-1, 4), n_work=int(work.shape[0]),
+            total_q=int(qo_indptr[-1]), page_size=P,
+        )
+
+    def _forward_prefill(self, q, k, v, layer_id: int, meta: B200PrefillMetadata) -> torch.Tensor:
+        T = meta.total_q
+        assert q.shape == (T, self.Hq, self.D), q.shape
+        q = q.contiguous()
+        out = torch.empty_like(q)
+        B = len(meta.q_offsets) - 1
+        nat.call(
+            "b2a_extend", q.data_ptr(), self.kv_cache.k_cache(layer_id).data_ptr(),
+            self.kv_cache.v_cache(layer_id).data_ptr(), self.kv_cache.num_tokens, meta.qo_indptr.data_ptr(),
+            meta.kv_indptr.data_ptr(), meta.kv_indices.data_ptr(), meta.kv_last_page_len.data_ptr(),
+            meta.page_size, meta.work.data_ptr(), meta.n_work, T, B, self.Hq, self.Hkv, self.D,
+            float(self.scale), out.data_ptr(), self.dtype_code, current_stream_ptr(self.device),
+        )
+        return out
+
+
+def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
+                           kv_indptr: torch.Tensor, kv_indices: torch.Tensor, scale) -> torch.Tensor:
+    """Same call as the reference's ``paged_decode_attention`` (attention/metal.py:112-131).
+
+    q ``[B, Hq, D]``; pools ``[N, Hkv, D]``; kv_indptr int32 ``[B+1]`` token CSR;
+    kv_indices int32 slots; scale a float or a 1-element tensor. One CTA per request
+    (``b2a_paged_decode``), no workspace.
+    """
+    B, Hq, D = q.shape
+    Hkv = k_pool.shape[1]
+    assert D % 32 == 0 and Hq % Hkv == 0
+    assert kv_indptr.dtype == torch.int32 and kv_indices.dtype == torch.int32
+    assert k_pool.is_contiguous() and v_pool.is_contiguous() and k_pool.shape == v_pool.shape
+    if isinstance(scale, torch.Tensor):
+        scale = float(scale.reshape(-1)[0].item())
+    q = q.contiguous()
+    out = torch.empty_like(q)
+    nat.call(
+        "b2a_paged_decode", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), k_pool.shape[0], kv_indptr.data_ptr(),
+        kv_indices.data_ptr(), B, Hq, Hkv, D, float(scale), out.data_ptr(), dtype_code(q.dtype),
+        current_stream_ptr(q.device),
+    )
+    return out

@@ -1,0 +1,88 @@
+"""GPU parity of ragged causal extend (prefill) attention against the oracle.
+
+The oracle is the reference's shared prefill (attention/base.py:107-142): per
+request SDPA, fresh k/v when nothing is cached, the pool rows of
+page_table[row, :device_len] otherwise, causal bottom-right when Lq > 1.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from helpers import TOL, HeadConfig, max_abs, rand, to_dev, to_np, torch_dtype
+from minisgl_b200 import workloads as W
+from oracle import attention as O
+
+pytestmark = pytest.mark.gpu
+
+
+def _run_extend(eb: W.ExtendBatch, Hq, Hkv, D, dtype, seed=0):
+    import torch
+
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.kvcache import MHAKVCache
+
+    pb = eb.paged
+    rng = np.random.default_rng(seed)
+    N = pb.num_slots
+    hk = rand(rng, (N, Hkv, D), dtype)
+    hv = rand(rng, (N, Hkv, D), dtype)
+    kv = MHAKVCache(1, N, Hkv, D, torch_dtype(dtype))
+    kv.k[0].copy_(torch.from_numpy(hk))
+    kv.v[0].copy_(torch.from_numpy(hv))
+    T = int(eb.extend.sum())
+    q = rand(rng, (T, Hq, D), dtype)
+    be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=pb.page_size)
+    meta = be.extend_metadata_from_lens(pb.rows, pb.lens, eb.extend)
+    out = be._forward_prefill(to_dev(q, dtype), None, None, 0, meta)
+    torch.cuda.synchronize()
+    # oracle: fresh k/v rows are the pool rows just stored at positions [prefix, len)
+    ks, vs = [], []
+    for b in range(pb.batch_size):
+        sl = pb.page_table[b, int(eb.prefix[b]):int(pb.lens[b])]
+        ks.append(hk[sl])
+        vs.append(hv[sl])
+    omet = O.prepare_prefill(pb.page_table, pb.rows, eb.prefix, pb.lens)
+    ref = O.forward_prefill(q, np.concatenate(ks), np.concatenate(vs), hk, hv, omet, D ** -0.5)
+    np.testing.assert_array_equal(to_np(meta.last_indices).astype(np.int64), omet.last_indices)
+    return to_np(out), ref
+
+
+def _batch(prefix, extend, P, seed=0, slots=None):
+    rng = np.random.default_rng(seed)
+    prefix = np.asarray(prefix, np.int64)
+    extend = np.asarray(extend, np.int64)
+    lens = prefix + extend
+    n = slots or int(((lens + P - 1) // P * P).sum() * 2 + 4 * P)
+    pb = W.allocate_pages(lens, n // P * P, P, rng)
+    return W.ExtendBatch(pb, prefix, extend)
+
+
+EDGE = dict(prefix=[0, 0, 5, 16, 100, 31, 700, 0], extend=[1, 7, 1, 64, 130, 2, 65, 200])
+
+
+@pytest.mark.parametrize("hq,hkv,d", [(16, 8, 128), (32, 8, 128), (8, 8, 64), (16, 2, 256)])
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("P", [1, 16])
+def test_extend_edge_cases(hq, hkv, d, dtype, P):
+    eb = _batch(EDGE["prefix"], EDGE["extend"], P, seed=1)
+    out, ref = _run_extend(eb, hq, hkv, d, dtype, seed=2)
+    err = max_abs(out, ref)
+    assert err <= TOL[dtype], err
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+def test_extend_config3_shapes(dtype):
+    """Config 3 (32 ragged requests, prefix U[0,4096] page-aligned + one unaligned,
+    extend U[64,512], 16/8/128, page 16), reduced to 8 requests for the fp64 oracle."""
+    eb = W.config3_batch(seed=0, batch=8)
+    out, ref = _run_extend(eb, 16, 8, 128, dtype, seed=4)
+    err = max_abs(out, ref)
+    assert err <= TOL[dtype], err
+
+
+def test_extend_single_request_long_prefix_bf16():
+    eb = _batch([4000], [512], 16, seed=3)
+    out, ref = _run_extend(eb, 16, 8, 128, "bfloat16", seed=5)
+    assert max_abs(out, ref) <= TOL["bfloat16"]
