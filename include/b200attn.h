@@ -146,11 +146,15 @@ int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t nu
  * b2a_extend_plan (host only) tiles every request into query tiles of
  * b2a_extend_tile_q() rows and orders them longest-first:
  *   work (out) : int32 [work_capacity * 4] = {request, q_tile_begin, q_tile_rows, 0}
- * The kernel is chosen by dtype/shape: bf16 with D == 128 runs on tcgen05
- * tensor cores (TMEM accumulators, TMA-fed tiles); every other supported
- * shape runs a SIMT fp32-accumulating kernel.
+ * The kernel is chosen by (dtype, D, Hq/Hkv, page_size): bf16 with D == 128,
+ * GQA group 1/2/4/8 and page_size a multiple of 16 runs on tcgen05 tensor
+ * cores (TMEM accumulators, TMA-fed tiles, 128/G query tokens per tile);
+ * every other supported shape runs a SIMT fp32-accumulating kernel (64/G
+ * tokens per tile). `work` must come from b2a_extend_plan with the tile size
+ * b2a_extend_tile_q returns for the same arguments; a larger tile is clamped
+ * and flagged through the watchdog word.
  * ------------------------------------------------------------------------ */
-int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int* tile_q);
+int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* tile_q);
 int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
                     const int32_t* kv_last_page_len, int B, int page_size, int tile_q,
                     int32_t* work, int work_capacity, int* n_work);

@@ -409,11 +409,17 @@ int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t nu
 }
 
 // ------------------------------------------------------------------ extend
-int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int* tile_q) {
+static bool extend_uses_tc(int Hq, int Hkv, int D, int dtype, int page_log2) {
+  return b2a::extend_tc_supported(Hq, Hkv, D, dtype) && b2a::extend_tc_page_ok(page_log2);
+}
+
+int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* tile_q) {
   if (!tile_q) return fail(B2A_ERR_INVALID, "tile_q is NULL");
   if (int rc = check_heads(Hq, Hkv, D)) return rc;
+  const int plog = ilog2_exact(page_size);
+  if (plog < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
   const int G = Hq / Hkv;
-  if (b2a::extend_tc_supported(Hq, Hkv, D, dtype)) {
+  if (extend_uses_tc(Hq, Hkv, D, dtype, plog)) {
     *tile_q = b2a::kTcRows / G;
   } else {
     if (G > b2a::kSimtRows) return fail(B2A_ERR_UNSUPPORTED, "GQA group %d too large", G);
@@ -477,7 +483,7 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
   if (dtype == B2A_DTYPE_F16 || dtype_size(dtype) == 0) return fail(B2A_ERR_UNSUPPORTED, "extend dtype %d", dtype);
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int G = Hq / Hkv;
-  if (b2a::extend_tc_supported(Hq, Hkv, D, dtype)) {
+  if (extend_uses_tc(Hq, Hkv, D, dtype, plog)) {
     return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
                                  plog, work, n_work, T, Hq, Hkv, scale, out, st, g_err);
   }

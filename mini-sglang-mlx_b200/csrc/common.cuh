@@ -25,6 +25,7 @@ enum WatchdogCode : int {
   kWdDecodeDrain = 3,
   kWdExtendBar = 16,
   kWdExtendDrain = 17,
+  kWdTileTooLarge = 33,  // a work tile larger than the kernel's tile: clamped
   kWdBadSlot = 32,  // a page id / slot outside the pool: access skipped
 };
 

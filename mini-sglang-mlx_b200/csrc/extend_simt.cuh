@@ -56,9 +56,11 @@ __global__ void __launch_bounds__(kSimtThreads) extend_simt_kernel(const ExtendA
   float* Vs = Ks + BK * (D + 1);       // [BK][D]
 
   const int4 w = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
-  const int r = w.x, tb = w.y, nq = w.z;
+  const int r = w.x, tb = w.y;
   const int h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nq = min(w.z, kSimtRows / G);
+  if (w.z > nq && tid == 0) watchdog_set(kWdTileTooLarge);
   const int Lq = a.qo_indptr[r + 1] - a.qo_indptr[r];
   const int Lkv = request_kv_len(a.kv_indptr, a.kv_last_page_len, r, a.page_log2);
   const int prefix = Lkv - Lq;

@@ -1,26 +1,528 @@
-// Ragged causal extend attention on tcgen05 tensor cores (bf16, head_dim 128).
+// Ragged causal extend attention on 5th-generation tensor cores (sm_100a).
+//
+// Reference: python/minisgl_mlx/attention/base.py:107-142 (per-request SDPA,
+// bottom-right causal). Same contract as extend_simt.cuh; this is the
+// bf16 / head_dim 128 / page_size % 16 == 0 path.
+//
+// CTA = (query tile, kv head h). The 128-row MMA tile packs 128/G query
+// tokens x the G query heads of kv head h (row = token * G + g), so one pass
+// over the K/V of head h serves the whole GQA group.
+//   warp 0     TMA producer: Q tile once (two 64-column SW128 boxes), then K and
+//              V blocks of 128 keys as 16-row boxes, one per 16 keys of a page
+//              (pages are gathered through kv_indices; keys past the sequence
+//              load from an out-of-range coordinate and arrive as zeros).
+//   warp 1     MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
+//              accumulator (kind::f16, M=128 N=128, fp32), then O += P V with
+//              P from shared memory (K-major) and V as an MN-major operand.
+//   warp 2     TMEM allocator (512 columns: S0, S1, O).
+//   warps 4-7  softmax / correction / epilogue: thread t owns TMEM lane t =
+//              tile row t, so row max and row sum need no cross-thread
+//              reduction. The running max is only moved when it grows by more
+//              than 8 (log2 units); otherwise p = 2^(s - m_stale) <= 256 keeps
+//              the accumulation exact in fp32 and O is not rescaled.
+// Every mbarrier wait is bounded; a wait that gives up records a watchdog
+// code, the roles unwind, in-flight copies and MMAs are drained (bounded) and
+// TMEM is released before the CTA exits.
 #pragma once
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
 #include <string>
 
 #include "common.cuh"
 
 namespace b2a {
 
-constexpr int kTcRows = 128;  // query rows (tokens x GQA heads) per CTA tile
+constexpr int kTcRows = 128;      // query rows (tokens x GQA heads) per CTA tile
+constexpr int kTcKeys = 128;      // keys per K/V block
+constexpr int kTcD = 128;         // head_dim handled by this kernel
+constexpr int kTcThreads = 256;   // 8 warps
+constexpr uint32_t kTcTileBytes = 128 * 128 * 2;  // one 128x128 bf16 tile (32 KB)
+constexpr uint32_t kTcHalfBytes = kTcTileBytes / 2;  // one 64-column SW128 half (16 KB)
 
-inline bool extend_tc_supported(int Hq, int Hkv, int D, int dtype) {
-  (void)Hq;
-  (void)Hkv;
-  (void)D;
-  (void)dtype;
+struct TcArgs {
+  const int32_t* qo_indptr;
+  const int32_t* kv_indptr;
+  const int32_t* kv_indices;
+  const int32_t* kv_last_page_len;
+  const int32_t* work;
+  __nv_bfloat16* out;
+  int64_t num_slots;
+  int page_log2;
+  int Hq, G;
+  float qscale;  // scale * log2(e)
+};
+
+// shared-memory map (offsets from a 1024-byte aligned base)
+struct TcSmem {
+  static constexpr uint32_t Q = 0;
+  static constexpr uint32_t K0 = Q + kTcTileBytes;
+  static constexpr uint32_t V0 = K0 + 2 * kTcTileBytes;
+  static constexpr uint32_t P = V0 + 2 * kTcTileBytes;
+  static constexpr uint32_t BARS = P + kTcTileBytes;
+  // barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, p_empty, o_full
+  static constexpr int NBARS = 16;
+  static constexpr uint32_t TMEM_SLOT = BARS + NBARS * 8;
+  static constexpr uint32_t ABORT = TMEM_SLOT + 8;
+  static constexpr uint32_t TOTAL = ABORT + 8;
+  static constexpr uint32_t ALLOC = TOTAL + 1024;  // slack for aligning the base
+};
+
+// ------------------------------------------------------------ PTX wrappers
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+               : "memory");
+}
+
+__device__ __forceinline__ void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+#define B2A_R32(X) \
+  "=r"(X[0]), "=r"(X[1]), "=r"(X[2]), "=r"(X[3]), "=r"(X[4]), "=r"(X[5]), "=r"(X[6]), "=r"(X[7]), "=r"(X[8]), \
+      "=r"(X[9]), "=r"(X[10]), "=r"(X[11]), "=r"(X[12]), "=r"(X[13]), "=r"(X[14]), "=r"(X[15]), "=r"(X[16]), \
+      "=r"(X[17]), "=r"(X[18]), "=r"(X[19]), "=r"(X[20]), "=r"(X[21]), "=r"(X[22]), "=r"(X[23]), "=r"(X[24]), \
+      "=r"(X[25]), "=r"(X[26]), "=r"(X[27]), "=r"(X[28]), "=r"(X[29]), "=r"(X[30]), "=r"(X[31])
+#define B2A_W32(X) \
+  "r"(X[0]), "r"(X[1]), "r"(X[2]), "r"(X[3]), "r"(X[4]), "r"(X[5]), "r"(X[6]), "r"(X[7]), "r"(X[8]), "r"(X[9]), \
+      "r"(X[10]), "r"(X[11]), "r"(X[12]), "r"(X[13]), "r"(X[14]), "r"(X[15]), "r"(X[16]), "r"(X[17]), "r"(X[18]), \
+      "r"(X[19]), "r"(X[20]), "r"(X[21]), "r"(X[22]), "r"(X[23]), "r"(X[24]), "r"(X[25]), "r"(X[26]), "r"(X[27]), \
+      "r"(X[28]), "r"(X[29]), "r"(X[30]), "r"(X[31])
+
+// 32 consecutive fp32 columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+      "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : B2A_R32(r)
+      : "r"(taddr));
+}
+
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31, %32};" ::"r"(taddr),
+      B2A_W32(r)
+      : "memory");
+}
+
+__device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+__device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor, SWIZZLE_128B (sm_100 encoding: version 1 at
+// bits 46-47, layout type 2 at bits 61-63). K-major tiles are rows of 128 B,
+// 8-row groups 1024 B apart (SBO); MN-major tiles add LBO = distance between
+// 64-element column chunks.
+__device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_bytes, uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor, kind::f16: bf16 x bf16 -> fp32, M=128, N=128.
+__host__ __device__ constexpr uint32_t tc_idesc(bool b_mn_major) {
+  return (1u << 4)                          // D format fp32
+         | (1u << 7)                        // A bf16
+         | (1u << 10)                       // B bf16
+         | ((b_mn_major ? 1u : 0u) << 16)   // B major
+         | ((uint32_t)(128 >> 3) << 17)     // N
+         | ((uint32_t)(128 >> 4) << 24);    // M
+}
+
+__device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag) {
+  if (*abort_flag) return false;
+  if (mbar_wait(bar, parity, kWdExtendBar)) return true;
+  *abort_flag = 1;
   return false;
 }
 
-inline int extend_tc_launch(const void*, const void*, const void*, int64_t, const int32_t*, const int32_t*,
-                            const int32_t*, const int32_t*, int, const int32_t*, int, int, int, int, float, void*,
-                            cudaStream_t, std::string& err) {
-  err = "tcgen05 extend kernel not built";
-  return 2;
+// ------------------------------------------------------------ kernel
+__global__ void __launch_bounds__(kTcThreads, 1)
+    extend_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                     const __grid_constant__ CUtensorMap vmap, const TcArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::BARS);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;   // [2]
+  uint64_t* k_empty = bars + 3;  // [2]
+  uint64_t* v_full = bars + 5;   // [2]
+  uint64_t* v_empty = bars + 7;  // [2]
+  uint64_t* s_full = bars + 9;   // [2]
+  uint64_t* s_empty = bars + 11; // [2]
+  uint64_t* p_full = bars + 13;
+  uint64_t* p_empty = bars + 14;
+  uint64_t* o_full = bars + 15;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::TMEM_SLOT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::ABORT);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int4 w = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
+  const int r = w.x, tb = w.y;
+  const int h = blockIdx.y;
+  const int G = a.G;
+  const int nq = min(w.z, kTcRows / G);
+  if (w.z > nq && threadIdx.x == 0) watchdog_set(kWdTileTooLarge);
+  const int P = 1 << a.page_log2;
+  const int q0 = a.qo_indptr[r];
+  const int Lq = a.qo_indptr[r + 1] - q0;
+  const int pbeg = a.kv_indptr[r];
+  const int npages = a.kv_indptr[r + 1] - pbeg;
+  const int Lkv = npages > 0 ? ((npages - 1) << a.page_log2) + (a.kv_last_page_len ? a.kv_last_page_len[r] : P) : 0;
+  const int prefix = Lkv - Lq;
+  const int kv_end = min(Lkv, prefix + tb + nq);  // keys visible to the last row of the tile
+  const int nb = (kv_end + kTcKeys - 1) / kTcKeys;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&k_full[i], 1);
+      mbar_init(&k_empty[i], 1);
+      mbar_init(&v_full[i], 1);
+      mbar_init(&v_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_empty[i], 128);
+    }
+    mbar_init(p_full, 128);
+    mbar_init(p_empty, 1);
+    mbar_init(o_full, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 2) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer
+    int issued_k = 0, issued_v = 0;
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, kTcTileBytes);
+      tma_load_3d(smem + TcSmem::Q, &qmap, 0, h * G, q0 + tb, q_full);
+      tma_load_3d(smem + TcSmem::Q + kTcHalfBytes, &qmap, 64, h * G, q0 + tb, q_full);
+    }
+    for (int j = 0; j < nb; ++j) {
+      const int st = j & 1;
+      const uint32_t ph = (uint32_t)(j >> 1) & 1u;
+      // lane l < 16: box b = l/2 (keys j*128 + 16b ..), column half l%2
+      int z = (int)a.num_slots;  // out of range -> zero fill
+      const int b = lane >> 1, half = lane & 1;
+      if (lane < 16) {
+        const int key0 = j * kTcKeys + b * 16;
+        if (key0 < Lkv) {
+          const int64_t page = a.kv_indices[pbeg + (key0 >> a.page_log2)];
+          const int64_t slot = page * P + (key0 & (P - 1));
+          if (page >= 0 && slot + 16 <= a.num_slots) z = (int)slot;
+          else watchdog_set(kWdBadSlot);
+        }
+      }
+      bool ok = __all_sync(0xffffffffu, tc_wait(&k_empty[st], ph ^ 1u, abort_flag));
+      if (!ok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&k_full[st], kTcTileBytes);
+      __syncwarp();
+      if (lane < 16)
+        tma_load_3d(smem + TcSmem::K0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &kmap, half * 64, h, z,
+                    &k_full[st]);
+      ++issued_k;
+      ok = __all_sync(0xffffffffu, tc_wait(&v_empty[st], ph ^ 1u, abort_flag));
+      if (!ok) break;
+      if (lane == 0) mbar_arrive_expect_tx(&v_full[st], kTcTileBytes);
+      __syncwarp();
+      if (lane < 16)
+        tma_load_3d(smem + TcSmem::V0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &vmap, half * 64, h, z,
+                    &v_full[st]);
+      ++issued_v;
+    }
+    // drain: our own copies must land before the CTA may exit
+    if (lane == 0) {
+      mbar_wait(q_full, 0, kWdExtendDrain);
+      for (int i = max(0, issued_k - 2); i < issued_k; ++i) mbar_wait(&k_full[i & 1], (uint32_t)(i >> 1) & 1u, kWdExtendDrain);
+      for (int i = max(0, issued_v - 2); i < issued_v; ++i) mbar_wait(&v_full[i & 1], (uint32_t)(i >> 1) & 1u, kWdExtendDrain);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_qk = tc_idesc(false);
+      constexpr uint32_t idesc_pv = tc_idesc(true);
+      const uint32_t sQ = smem_u32(smem + TcSmem::Q);
+      const uint32_t sP = smem_u32(smem + TcSmem::P);
+      bool ok = tc_wait(q_full, 0, abort_flag);
+      auto issue_pv = [&](int i) -> bool {
+        const int vs = i & 1;
+        if (!tc_wait(p_full, (uint32_t)i & 1u, abort_flag)) return false;
+        if (!tc_wait(&v_full[vs], (uint32_t)(i >> 1) & 1u, abort_flag)) return false;
+        tc_fence_after();
+        const uint32_t sV = smem_u32(smem + TcSmem::V0 + vs * kTcTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sw128_desc(sP + (kk >> 2) * kTcHalfBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(sV + kk * 2048, kTcHalfBytes, 1024);
+          tc_mma_f16(tO, ad, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        tc_commit(p_empty);
+        tc_commit(&v_empty[vs]);
+        return true;
+      };
+      for (int j = 0; j < nb && ok; ++j) {
+        const int ks = j & 1;
+        const uint32_t kph = (uint32_t)(j >> 1) & 1u;
+        if (!tc_wait(&k_full[ks], kph, abort_flag) || !tc_wait(&s_empty[ks], kph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t sK = smem_u32(smem + TcSmem::K0 + ks * kTcTileBytes);
+        const uint32_t tS = ks ? tS1 : tS0;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = sw128_desc(sQ + (kk >> 2) * kTcHalfBytes + (kk & 3) * 32, 16, 1024);
+          const uint64_t bd = sw128_desc(sK + (kk >> 2) * kTcHalfBytes + (kk & 3) * 32, 16, 1024);
+          tc_mma_f16(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(&s_full[ks]);
+        tc_commit(&k_empty[ks]);
+        if (j >= 1 && !issue_pv(j - 1)) {
+          ok = false;
+          break;
+        }
+      }
+      if (ok && nb > 0) ok = issue_pv(nb - 1);
+      tc_commit(o_full);  // also fires (with whatever O holds) on the abort path, so nobody waits forever
+      // drain: every MMA we issued has completed once o_full has fired
+      mbar_wait(o_full, 0, kWdExtendDrain);
+    }
+  } else if (warp >= 4) {
+    // ---------------------------------------------------------------- softmax + epilogue
+    // tcgen05.ld/st are warp-collective (.sync.aligned): every branch around
+    // them below is warp-uniform (decided with __all_sync / __any_sync).
+    constexpr unsigned FULL = 0xffffffffu;
+    const int row = threadIdx.x - 128;  // == TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int tok = row / G;
+    const int qpos = prefix + tb + tok;  // absolute position of this row's query token
+    float m = kNegInf, l = 0.f;
+    uint8_t* sP = smem + TcSmem::P;
+    bool ok = true;
+    for (int j = 0; j < nb; ++j) {
+      const int sb = j & 1;
+      ok = __all_sync(FULL, tc_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, abort_flag));
+      if (!ok) break;
+      tc_fence_after();
+      float s[128];
+      {
+        uint32_t u[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32((sb ? tS1 : tS0) + lane_off + c * 32, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(u[i]);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(&s_empty[sb]);
+      // scale into the log2 domain and apply the causal / length mask
+      const int kbase = j * kTcKeys;
+      const int limit = min(qpos, Lkv - 1) - kbase;  // keys 0..limit of this block are visible
+      float mx = kNegInf;
+#pragma unroll
+      for (int c = 0; c < 128; ++c) {
+        const float v = (c <= limit) ? s[c] * a.qscale : kNegInf;
+        s[c] = v;
+        mx = fmaxf(mx, v);
+      }
+      const float m_new = fmaxf(m, mx);
+      float alpha = 1.f;
+      if (m == kNegInf) {
+        m = m_new;  // first visible keys: nothing accumulated yet
+      } else if (m_new - m > 8.f) {
+        alpha = exp2f(m - m_new);
+        m = m_new;
+      }
+      // P buffer and O are free once PV of the previous block has completed
+      if (j >= 1) {
+        ok = __all_sync(FULL, tc_wait(p_empty, (uint32_t)(j - 1) & 1u, abort_flag));
+        if (!ok) break;
+        tc_fence_after();
+        if (__any_sync(FULL, alpha != 1.f)) {
+          uint32_t u[32];
+#pragma unroll
+          for (int c = 0; c < 4; ++c) {
+            tmem_ld32(tO + lane_off + c * 32, u);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+            tmem_st32(tO + lane_off + c * 32, u);
+          }
+          tmem_wait_st();
+        }
+      }
+      float psum = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < 16; ++ch) {
+        uint32_t pk[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const float p0 = (s[ch * 8 + 2 * e] == kNegInf) ? 0.f : exp2f(s[ch * 8 + 2 * e] - m);
+          const float p1 = (s[ch * 8 + 2 * e + 1] == kNegInf) ? 0.f : exp2f(s[ch * 8 + 2 * e + 1] - m);
+          psum += p0 + p1;
+          __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
+          pk[e] = *reinterpret_cast<uint32_t*>(&pp);
+        }
+        const int half = ch >> 3, c8 = ch & 7;
+        uint8_t* dst = sP + half * kTcHalfBytes + row * 128 + ((c8 ^ (row & 7)) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+      }
+      l = l * alpha + psum;
+      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+      tc_fence_before();
+      mbar_arrive(p_full);
+    }
+    // ---- epilogue: O / l -> bf16 rows of the output
+    const bool got_o = __all_sync(FULL, mbar_wait(o_full, 0, kWdExtendBar));
+    tc_fence_after();
+    if (ok && got_o) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int g = row - tok * G;
+      __nv_bfloat16* dst = a.out + ((size_t)(q0 + tb + tok) * a.Hq + h * G + g) * kTcD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        tmem_ld32(tO + lane_off + c * 32, u);
+        tmem_wait_ld();
+        uint32_t pk[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
+          pk[i] = *reinterpret_cast<uint32_t*>(&pp);
+        }
+        if (tok < nq) {  // rows past the tile's end are computed but never stored
+          uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(512) : "memory");
+  }
+}
+
+// ------------------------------------------------------------ host side
+inline bool extend_tc_supported(int Hq, int Hkv, int D, int dtype) {
+  const int G = Hkv > 0 ? Hq / Hkv : 0;
+  return dtype == 1 /* bf16 */ && D == kTcD && (G == 1 || G == 2 || G == 4 || G == 8);
+}
+
+// Page sizes the TMA gather handles (16-row boxes inside one page).
+inline bool extend_tc_page_ok(int page_log2) { return page_log2 >= 4; }
+
+inline PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder(std::string& err) {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn) return fn;
+  void* p = nullptr;
+  cudaDriverEntryPointQueryResult q;
+  cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q);
+  if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !p) {
+    err = "cuTensorMapEncodeTiled entry point unavailable";
+    return nullptr;
+  }
+  fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  return fn;
+}
+
+inline bool encode_3d(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, const void* base, uint64_t d0,
+                      uint64_t d1, uint64_t d2, uint64_t stride1_bytes, uint64_t stride2_bytes, uint32_t b0,
+                      uint32_t b1, uint32_t b2) {
+  cuuint64_t dims[3] = {d0, d1, d2};
+  cuuint64_t strides[2] = {stride1_bytes, stride2_bytes};
+  cuuint32_t box[3] = {b0, b1, b2};
+  cuuint32_t estr[3] = {1, 1, 1};
+  CUresult rc = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return rc == CUDA_SUCCESS;
+}
+
+inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                            const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
+                            const int32_t* kv_last_page_len, int page_log2, const int32_t* work, int n_work, int T,
+                            int Hq, int Hkv, float scale, void* out, cudaStream_t st, std::string& err) {
+  const int G = Hq / Hkv;
+  auto enc = tensor_map_encoder(err);
+  if (!enc) return 3;
+  if (T <= 0 || num_slots <= 0 || num_slots > 0x7fffffffLL - 64) {
+    err = "extend_tc: T and num_slots must be in (0, 2^31)";
+    return 1;
+  }
+  CUtensorMap qm, km, vm;
+  const uint64_t row = (uint64_t)kTcD * 2;
+  if (!encode_3d(enc, &qm, q, kTcD, (uint64_t)Hq, (uint64_t)T, row, row * Hq, 64, (uint32_t)G,
+                 (uint32_t)(kTcRows / G)) ||
+      !encode_3d(enc, &km, k_pool, kTcD, (uint64_t)Hkv, (uint64_t)num_slots, row, row * Hkv, 64, 1, 16) ||
+      !encode_3d(enc, &vm, v_pool, kTcD, (uint64_t)Hkv, (uint64_t)num_slots, row, row * Hkv, 64, 1, 16)) {
+    err = "extend_tc: cuTensorMapEncodeTiled rejected a tensor map";
+    return 1;
+  }
+  TcArgs a;
+  a.qo_indptr = qo_indptr;
+  a.kv_indptr = kv_indptr;
+  a.kv_indices = kv_indices;
+  a.kv_last_page_len = kv_last_page_len;
+  a.work = work;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.num_slots = num_slots;
+  a.page_log2 = page_log2;
+  a.Hq = Hq;
+  a.G = G;
+  a.qscale = scale * kLog2e;
+  cudaError_t e = cudaFuncSetAttribute(extend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)TcSmem::ALLOC);
+  if (e != cudaSuccess) {
+    err = std::string("extend_tc: smem attribute: ") + cudaGetErrorString(e);
+    return 3;
+  }
+  extend_tc_kernel<<<dim3(n_work, Hkv), kTcThreads, TcSmem::ALLOC, st>>>(qm, km, vm, a);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) {
+    err = std::string("extend_tc_kernel: ") + cudaGetErrorString(e);
+    return 3;
+  }
+  err.clear();
+  return 0;
 }
 
 }  // namespace b2a

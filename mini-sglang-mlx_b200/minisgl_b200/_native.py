@@ -62,7 +62,7 @@ SIGNATURES = {
         [_P, _P, _P, c_int64, _P, c_int, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_float,
          _P, c_size_t, _P, c_int, _P],
     ),
-    "b2a_extend_tile_q": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
+    "b2a_extend_tile_q": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
     "b2a_extend_plan": (
         c_int,
         [_P, _P, _P, c_int, c_int, c_int, _P, c_int, ctypes.POINTER(c_int)],
@@ -139,9 +139,9 @@ def decode_plan(kv_indptr: np.ndarray, kv_last_page_len: np.ndarray | None, page
     return cta_indptr, segs[: 4 * n_segs.value].reshape(-1, 4), merge_indptr, n_part.value
 
 
-def extend_tile_q(Hq: int, Hkv: int, D: int, dtype_code: int) -> int:
+def extend_tile_q(Hq: int, Hkv: int, D: int, dtype_code: int, page_size: int) -> int:
     t = c_int(0)
-    call("b2a_extend_tile_q", Hq, Hkv, D, dtype_code, ctypes.byref(t))
+    call("b2a_extend_tile_q", Hq, Hkv, D, dtype_code, page_size, ctypes.byref(t))
     return t.value
 
 

@@ -80,7 +80,6 @@ class B200AttnBackend(BaseAttnBackend):
         with torch.cuda.device(self.device):
             nat.call("b2a_decode_num_ctas", self.Hq, self.Hkv, self.D, self.dtype_code, nat.ctypes.byref(n))
         self.num_ctas = n.value
-        self.tile_q = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code)
 
     # ------------------------------------------------------------ helpers
     @property
@@ -144,7 +143,8 @@ class B200AttnBackend(BaseAttnBackend):
         qo_indptr = np.zeros(len(extend) + 1, np.int32)
         np.cumsum(extend, out=qo_indptr[1:])
         kv_indptr, kv_indices, lpl = paged_kv_indices(self.page_table, rows, lens, P, check=CHECK_METADATA)
-        work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, self.tile_q)
+        tile_q = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code, P)
+        work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
         dev = self._stager.upload([last_indices, qo_indptr, kv_indptr, kv_indices, lpl, work], self.device)
         return B200PrefillMetadata(
