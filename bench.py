@@ -28,9 +28,7 @@ import datetime
 import json
 import os
 import statistics
-import subprocess
 import sys
-import tempfile
 import time
 from pathlib import Path
 
@@ -52,6 +50,9 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--layers", type=int, default=None,
+                    help="decode layers per step (default 28 = config 2); fewer only for profiling captures")
+    ap.add_argument("--no-extend", action="store_true", help="skip the config-3 extend measurement")
     return ap.parse_args()
 
 
@@ -65,51 +66,60 @@ def measured_peaks():
 
 # ------------------------------------------------------------------ clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and throttle reasons through NVML every 10 ms while running.
 
-    def __init__(self, gpu_index: int):
+    Read-only: no clock, power or mode setting of the GPU is touched.
+    """
+
+    REASONS = {  # NVML clocks-event-reason bits
+        "sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+        "hw_thermal_slowdown": 0x40, "hw_power_brake_slowdown": 0x80,
+    }
+
+    def __init__(self, gpu_index: int, period_s: float = 0.01):
         self.gpu = gpu_index
-        self.proc = None
-        self.file = None
+        self.period = period_s
+        self.samples = []
+        self._stop = None
+        self._thread = None
+        self._err = None
 
     def start(self):
+        import threading
+
         try:
-            self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=self.file, stderr=subprocess.DEVNULL)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            self._max = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # noqa: BLE001 - report, never fail the bench on telemetry
+            self._err = f"nvml unavailable: {e}"
+            return
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                try:
+                    sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                    self.samples.append((sm, rs))
+                except Exception:  # noqa: BLE001
+                    pass
+                time.sleep(self.period)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
 
     def stop(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        self.proc.terminate()
-        try:
-            self.proc.wait(timeout=5)
-        except subprocess.TimeoutExpired:
-            self.proc.kill()
-        self.file.flush()
-        self.file.seek(0)
-        sms, maxes, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.file.read().splitlines():
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sms.append(float(parts[1]))
-                maxes.append(float(parts[2]))
-            except ValueError:
-                continue
-            for n, v in zip(names, parts[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        os.unlink(self.file.name)
-        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
-                "reasons": sorted(reasons), "samples": len(sms)}
+        if self._thread is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self._err or "no samples"]}
+        self._stop.set()
+        self._thread.join()
+        sms = [s for s, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": self._max,
+                "reasons": reasons, "samples": len(sms), "source": "nvml 10 ms"}
 
 
 # ------------------------------------------------------------------ workload
@@ -148,6 +158,75 @@ def cpu_sample(lens, page_table, P, Hq, Hkv, D, num_slots, steps, warmup, seed):
     per_call = float(np.mean(times))
     gbs = decode_bytes(lens, P, Hq, Hkv, D, 2) / per_call / 1e9
     return gbs, per_call, torch.get_num_threads()
+
+
+def extend_flops(prefix: np.ndarray, extend: np.ndarray, Hq: int, D: int) -> float:
+    """Causal extend FLOPs: 2 GEMMs x 2 flops x Hq x D x visible keys of every query row."""
+    vis = sum(int(e) * int(p) + int(e) * (int(e) + 1) // 2 for p, e in zip(prefix, extend))
+    return 4.0 * Hq * D * vis
+
+
+def measure_extend(dev, seed: int, steps: int, warmup: int):
+    """Config 3: 32 ragged requests with a cached radix prefix, fused RoPE+store then extend attention."""
+    import torch
+
+    from minisgl_b200 import MHAKVCache
+    from minisgl_b200 import workloads as W
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.config import qwen3_0_6b
+    from minisgl_b200.layers import RotaryEmbedding
+
+    cfg = qwen3_0_6b()
+    Hq, Hkv, D = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim
+    eb = W.config3_batch(seed=seed)
+    pb = eb.paged
+    kv = MHAKVCache(1, pb.num_slots, Hkv, D, torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    kv.k[0].normal_(generator=gen)
+    kv.v[0].normal_(generator=gen)
+    be = B200AttnBackend(cfg, kv, pb.page_table, page_size=pb.page_size)
+    meta = be.extend_metadata_from_lens(pb.rows, pb.lens, eb.extend)
+    T = int(eb.extend.sum())
+    q = torch.randn((T, Hq, D), device=dev, generator=gen).to(torch.bfloat16)
+    knew = torch.randn((T, Hkv, D), device=dev, generator=gen).to(torch.bfloat16)
+    vnew = torch.randn((T, Hkv, D), device=dev, generator=gen).to(torch.bfloat16)
+    pos = np.concatenate([np.arange(p, p + e, dtype=np.int32) for p, e in zip(eb.prefix, eb.extend)])
+    rows = np.repeat(pb.rows, eb.extend)
+    loc = pb.page_table[rows, pos].astype(np.int32)
+    pos_t, loc_t = torch.from_numpy(pos).to(dev), torch.from_numpy(loc).to(dev)
+    rope = RotaryEmbedding(cfg.rotary_config, device=dev)
+    for _ in range(max(warmup, 3)):
+        rope.rope_store_(q, knew, vnew, pos_t, loc_t, kv, 0)
+        be._forward_prefill(q, None, None, 0, meta)
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        rope.rope_store_(q, knew, vnew, pos_t, loc_t, kv, 0)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        be._forward_prefill(q, None, None, 0, meta)
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    flops = extend_flops(eb.prefix, eb.extend, Hq, D)
+    peak = 1636.1
+    pk = ROOT / "MEASURED_PEAKS.json"
+    kind = "fallback"
+    if pk.exists():
+        peak, kind = float(json.loads(pk.read_text())["bf16_tflops"]), "measured"
+    tf = flops / (ms * 1e-3) / 1e12
+    from minisgl_b200 import _native as nat
+
+    tile = nat.extend_tile_q(Hq, Hkv, D, nat.B2A_DTYPE_BF16, pb.page_size)
+    return {"metric": "extend attention TFLOP/s (causal, visible keys only)", "value": round(tf, 2),
+            "unit": "TFLOP/s", "ms_per_call": round(ms, 4), "flops_per_call": flops,
+            "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(tf / peak, 4), "peak_kind": kind + " (bf16 dense, burst)"},
+            "config": {"workload": "config3: 32 ragged requests, prefix U[0,4096] page-aligned (+1 unaligned), "
+                                   "extend U[64,512], 16q/8kv/128, bf16, page 16, RoPE theta 1e6 fused store",
+                       "tokens": T, "sum_prefix": int(eb.prefix.sum()), "tile_q_tokens": tile,
+                       "kernel": "extend_tc_kernel (tcgen05)" if tile == 128 // (Hq // Hkv) else "extend_simt_kernel"}}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -198,7 +277,8 @@ def run_ours(args):
 
     c = W.CONFIG2
     cfg = qwen3_0_6b()
-    Lyr, Hq, Hkv, D, P, N = c["layers"], cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim, c["page_size"], c["num_slots"]
+    Lyr = args.layers or c["layers"]
+    Hq, Hkv, D, P, N = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim, c["page_size"], c["num_slots"]
     pb = W.config2_batch(seed=args.seed + 1000 * rank)
     B = pb.batch_size
 
@@ -327,6 +407,8 @@ def run_ours(args):
     achieved = dbytes / (dec_avg * 1e-3) / 1e9
     launches_per_step = Lyr * (2 + (1 if meta.n_partials > 0 else 0))
 
+    ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
+
     line = None
     if rank == 0:
         cpu = None
@@ -346,7 +428,7 @@ def run_ours(args):
                             "fragmented pages); per layer fused RoPE+KV store + split-KV decode",
                 "global_batch": B * world, "seq_len": "U[100,2048]", "parallelism": f"request-partitioned x{world}",
                 "l2": "inputs larger than L2 (each layer's ~560 MB KV working set > 126 MB L2)",
-                "sum_ctx_tokens_per_gpu": int(pb.lens.sum()),
+                "sum_ctx_tokens_per_gpu": int(pb.lens.sum()), "layers": Lyr,
             },
             "roofline": {
                 "bound": "hbm", "kernel": "decode_kernel+decode_merge_kernel (one b2a_decode call)",
@@ -362,6 +444,8 @@ def run_ours(args):
         }
         if cpu is not None:
             line["cpu_baseline"] = cpu
+        if ext is not None:
+            line["extend_config3"] = ext
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
