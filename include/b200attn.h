@@ -136,6 +136,29 @@ int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t nu
                void* stream);
 
 /* ------------------------------------------------------------------------
+ * Paged split-KV decode that allocates nothing and takes no workspace.
+ * No counterpart in the reference: it is an extra entry point of this
+ * library. It is for callers that cannot allocate device memory when decode
+ * runs, for example an engine whose memory planner has given the device to
+ * the KV pool, or a host that may only pass buffers it already owns.
+ * Same arguments and results as b2a_decode without workspace/workspace_bytes.
+ * The split partials live in an 8 MiB file-scope device array inside the
+ * library, held by every GPU that loads it until the process exits; a plan
+ * whose b2a_decode_workspace_bytes(n_partials, Hq, D) exceeds 8 MiB is
+ * rejected with B2A_ERR_WORKSPACE. The first call on a device looks up that
+ * array's device address (cudaGetSymbolAddress) with the device current; make
+ * that first call before any stream capture. All calls share the array and it
+ * keeps the last call's contents, so calls that overlap on the GPU (other
+ * streams, other host threads) race; serialise them. Nothing in the array has
+ * to start at zero.
+ * ------------------------------------------------------------------------ */
+int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                       const int32_t* kv_indices, int page_size, const int32_t* cta_indptr,
+                       const int32_t* segs, int num_ctas, const int32_t* merge_indptr,
+                       int n_partials, int B, int Hq, int Hkv, int D, float scale, void* out,
+                       int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * Ragged causal extend (prefill) attention over a paged prefix.
  * Replaces BaseAttnBackend._prepare_prefill/_forward_prefill
  * (python/minisgl_mlx/attention/base.py:107-142): request r owns query rows

@@ -408,6 +408,60 @@ int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t nu
                        n_partials, B, Hq, Hkv, D, scale, workspace, workspace_bytes, out, dtype, stream);
 }
 
+}  // extern "C"
+
+// ------------------------------------------------------------------ decode without allocation
+// Some callers cannot allocate device memory at the point where they run
+// decode: an engine whose memory planner has handed the whole device to the
+// KV pool, or a host that is only allowed to pass pointers it already owns
+// (pre-registered buffers, a foreign framework's tensors). For them the
+// split-KV partials live in this file-scope device array instead of a
+// caller-provided workspace. The array is part of the library image, so every
+// GPU that loads the library keeps it until the process exits.
+namespace {
+
+constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // 8 MiB of split partials per device
+__device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
+
+constexpr int kMaxDevices = 64;
+void* g_decode_scratch_addr[kMaxDevices] = {};  // device address of g_decode_scratch, per device
+
+}  // namespace
+
+extern "C" int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                                  const int32_t* kv_indices, int page_size, const int32_t* cta_indptr,
+                                  const int32_t* segs, int num_ctas, const int32_t* merge_indptr, int n_partials,
+                                  int B, int Hq, int Hkv, int D, float scale, void* out, int dtype, void* stream) {
+  if (!cta_indptr || !segs || num_ctas <= 0) return fail(B2A_ERR_INVALID, "decode plan missing (cta_indptr/segs)");
+  if (!aligned(segs, 16)) return fail(B2A_ERR_INVALID, "segs must be 16-byte aligned (read as int4)");
+  const size_t need = b2a_decode_workspace_bytes(n_partials, Hq, D);
+  if (need > kNoAllocScratchBytes)
+    return fail(B2A_ERR_WORKSPACE,
+                "b2a_decode_noalloc: %d split partials need %zu bytes, above the %zu-byte static scratch; "
+                "use b2a_decode with a workspace or a plan with fewer CTAs",
+                n_partials, need, kNoAllocScratchBytes);
+  int dev = -1;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
+    return fail(B2A_ERR_CUDA, "b2a_decode_noalloc: no usable current device (%s)", cudaGetErrorString(e));
+  if (!g_decode_scratch_addr[dev]) {
+    // One-time set-up on this device (the device is current here): the host
+    // symbol is only a stand-in, the kernel needs the device address.
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_decode_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(B2A_ERR_CUDA, "b2a_decode_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
+    g_decode_scratch_addr[dev] = p;
+  }
+  // The merge kernel reads only partial rows the decode kernel wrote in the
+  // same call, so nothing in the scratch has to start at zero.
+  return decode_common(q, k_pool, v_pool, num_slots, kv_indices, nullptr, page_size, cta_indptr, segs, num_ctas,
+                       merge_indptr, n_partials, B, Hq, Hkv, D, scale, g_decode_scratch_addr[dev],
+                       kNoAllocScratchBytes, out, dtype, stream);
+}
+
+extern "C" {
+
 // ------------------------------------------------------------------ extend
 static bool extend_uses_tc(int Hq, int Hkv, int D, int dtype, int page_log2) {
   return b2a::extend_tc_supported(Hq, Hkv, D, dtype) && b2a::extend_tc_page_ok(page_log2);

@@ -62,6 +62,11 @@ SIGNATURES = {
         [_P, _P, _P, c_int64, _P, c_int, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_float,
          _P, c_size_t, _P, c_int, _P],
     ),
+    "b2a_decode_noalloc": (
+        c_int,
+        [_P, _P, _P, c_int64, _P, c_int, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_float,
+         _P, c_int, _P],
+    ),
     "b2a_extend_tile_q": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
     "b2a_extend_plan": (
         c_int,
