@@ -124,34 +124,39 @@ struct DecodeCfg {
 constexpr size_t kSmemLimit = 232448;  // opt-in dynamic shared memory per block (sm_100)
 
 int decode_config(int Hq, int Hkv, int D, size_t es, DecodeCfg& c) {
-  if (Hkv > 8 || 8 % Hkv != 0)
-    return fail(B2A_ERR_UNSUPPORTED, "decode supports Hkv in {1, 2, 4, 8}, got %d", Hkv);
+  if (Hkv > 16 || 16 % Hkv != 0)
+    return fail(B2A_ERR_UNSUPPORTED, "decode supports Hkv in {1, 2, 4, 8, 16}, got %d", Hkv);
   const int G = Hq / Hkv;
-  c.WPH = 8 / Hkv;
-  c.NCW = 8;
+  const int TG = G <= 4 ? 8 : 32 / G;
   c.row_bytes = (uint32_t)(Hkv * D * es);
   int TS = 64;
   while (TS > 1 && 2ull * TS * c.row_bytes > 65536ull) TS >>= 1;
-  for (;;) {
-    c.TS = TS;
-    c.stage_bytes = (uint32_t)TS * c.row_bytes;
-    const b2a::DecodeSmem fixed = b2a::decode_smem_layout(0, 0, c.NCW, c.WPH, G, D);
+  // Prefer 16 consumer warps (two groups per head in flight); fall back to 8
+  // when a stage cannot feed them or the combine buffer does not fit.
+  for (int ncw : {16, 8}) {
+    if (ncw % Hkv != 0) continue;
+    const int wph = ncw / Hkv;
+    // 16 warps leave 96 registers a thread: only the shapes that fit them
+    if (ncw == 16 && (TS < wph * TG || D > 128 || G > 4)) continue;
+    const b2a::DecodeSmem fixed = b2a::decode_smem_layout(0, 0, ncw, wph, G, D);
+    const uint32_t stage = (uint32_t)TS * c.row_bytes;
     const size_t avail = kSmemLimit - fixed.total - 256;
-    int ns = (int)std::min<size_t>(4, avail / (2ull * c.stage_bytes));
-    if (ns >= 2 || TS == 1) {
-      c.NSTAGE = std::max(ns, 1);
-      break;
-    }
-    TS >>= 1;
+    const int ns = (int)std::min<size_t>(4, avail / (2ull * stage));
+    if (ns < 2) continue;
+    c.NCW = ncw;
+    c.WPH = wph;
+    c.TS = TS;
+    c.NSTAGE = ns;
+    c.stage_bytes = stage;
+    c.smem = b2a::decode_smem_layout(ns, stage, ncw, wph, G, D).total;
+    return B2A_OK;
   }
-  c.smem = b2a::decode_smem_layout(c.NSTAGE, c.stage_bytes, c.NCW, c.WPH, G, D).total;
-  if (c.smem > kSmemLimit) return fail(B2A_ERR_UNSUPPORTED, "decode config does not fit in shared memory");
-  return B2A_OK;
+  return fail(B2A_ERR_UNSUPPORTED, "decode config (Hq %d, Hkv %d, D %d) does not fit in shared memory", Hq, Hkv, D);
 }
 
-template <typename T, int D, int G>
+template <typename T, int D, int G, int NCW>
 int decode_launch(const b2a::DecodeArgs& a, const DecodeCfg& c, int grid, cudaStream_t st) {
-  auto kern = b2a::decode_kernel<T, D, G>;
+  auto kern = b2a::decode_kernel<T, D, G, NCW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
   if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "decode: set smem attribute: %s", cudaGetErrorString(e));
   kern<<<grid, (c.NCW + 1) * 32, c.smem, st>>>(a);
@@ -376,7 +381,13 @@ static int decode_common(const void* q, const void* k_pool, const void* v_pool, 
       constexpr int Dc = decltype(dc)::value;
       return with_g<Dc>(G, [&](auto gc) {
         constexpr int Gc = decltype(gc)::value;
-        if (int r = decode_launch<Tt, Dc, Gc>(a, c, grid, st)) return r;
+        int r;
+        if constexpr (Dc <= 128 && Gc <= 4) {
+          r = c.NCW == 16 ? decode_launch<Tt, Dc, Gc, 16>(a, c, grid, st) : decode_launch<Tt, Dc, Gc, 8>(a, c, grid, st);
+        } else {
+          r = decode_launch<Tt, Dc, Gc, 8>(a, c, grid, st);
+        }
+        if (r) return r;
         if (n_partials > 0) {
           const int blocks = (B * Hq + 3) / 4;
           b2a::decode_merge_kernel<Tt, Dc><<<blocks, 128, 0, st>>>(a.ws_acc, a.ws_ml, merge_indptr, out, B, Hq);

@@ -14,12 +14,15 @@
 //     concatenated page stream of the batch (host plan). A request cut by a
 //     share boundary produces partial (m, l, acc) rows that a merge kernel
 //     combines; requests inside a share are written directly.
-//   * Consumer warp w serves kv head w / WPH. Lane = D/32 features. The G
-//     query heads of the group share every K/V row read. Per group of 32/G
-//     tokens the G*32/G = 32 partial dot products are reduced with a
-//     transpose-butterfly (31 shuffles for 32 sums), leaving lane l with the
-//     score of (token l/G, head l%G); softmax statistics are per lane, the
-//     probabilities go through a 32-float smem slot to the PV loop.
+//   * NCW consumer warps (16 when shared memory allows, else 8); warp w
+//     serves kv head w / WPH and every WPH-th group of TG tokens of a stage,
+//     so two or more groups are in flight per head. Lane = D/32 features. The
+//     G query heads of the group share every K/V row read. The TG*G partial
+//     dot products of a group are reduced with a transpose-butterfly (about
+//     one shuffle per sum), leaving each lane with one (token, head) score;
+//     softmax statistics are per lane and the probabilities go through a
+//     32-float smem slot to the PV loop. Warps of one head combine their
+//     (m, l, acc) through shared memory at the end of a segment.
 //   * Scores are kept in the log2 domain (q pre-scaled by scale*log2 e).
 #pragma once
 #include <type_traits>
@@ -110,21 +113,25 @@ __device__ __forceinline__ void load_p(const float* pb, int i, float (&pg)[G]) {
   }
 }
 
-// One group of TG = 32/G tokens of the current stage for one kv head.
-template <typename T, int D, int G>
-__device__ __forceinline__ void decode_group(const T* __restrict__ Ks, const T* __restrict__ Vs, int t0,
-                                             int nvalid, int h, int Hkv, int lane,
-                                             const float (&qv)[G][D / 32], float (&acc)[G][D / 32],
-                                             float& m_mine, float& l_mine, float* pb) {
+// Tokens per reduction group: V = TG * G partial dot products per group,
+// V <= 32 so one lane ends up owning one (token, query head) score.
+template <int G>
+__host__ __device__ constexpr int decode_tg() {
+  return G <= 4 ? 8 : 32 / G;
+}
+
+constexpr int ilog2c(int x) { return x <= 1 ? 0 : 1 + ilog2c(x >> 1); }
+
+// Partial dot products of TG tokens x G query heads for one kv head.
+template <typename T, int D, int G, int TG, bool CHECK>
+__device__ __forceinline__ void decode_qk(const T* __restrict__ kh, int row_elems, int nvalid,
+                                          const float (&qv)[G][D / 32], float (&v)[TG * G]) {
   constexpr int EPT = D / 32;
-  constexpr int TG = 32 / G;
-  constexpr unsigned FULL = 0xffffffffu;
-  float v[32];
 #pragma unroll
   for (int i = 0; i < TG; ++i) {
-    if (i < nvalid) {
+    if (!CHECK || i < nvalid) {
       float kf[EPT];
-      load_vec<T, EPT>(Ks + ((size_t)(t0 + i) * Hkv + h) * D + lane * EPT, kf);
+      load_vec<T, EPT>(kh + i * row_elems, kf);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
         float s = 0.f;
@@ -137,45 +144,17 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ Ks, const T* 
       for (int g = 0; g < G; ++g) v[i * G + g] = 0.f;
     }
   }
-  // Transpose-butterfly: after the step with offset `off`, lanes with that bit
-  // set keep the upper half of the remaining values. Lane l ends holding the
-  // full sum of value l.
-#pragma unroll
-  for (int off = 16; off >= 1; off >>= 1) {
-    const bool upper = (lane & off) != 0;
-#pragma unroll
-    for (int j = 0; j < off; ++j) {
-      const float lo = v[j], hi = v[j + off];
-      const float send = upper ? lo : hi;
-      const float keep = upper ? hi : lo;
-      v[j] = keep + __shfl_xor_sync(FULL, send, off);
-    }
-  }
-  const int my_tok = lane / G;
-  const float s = (my_tok < nvalid) ? v[0] : kNegInf;
-  float mt = s;
-#pragma unroll
-  for (int off = G; off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(FULL, mt, off));
-  const float m_new = fmaxf(m_mine, mt);
-  const float alpha = (m_mine == m_new) ? 1.f : exp2f(m_mine - m_new);
-  const float p = (s == kNegInf) ? 0.f : exp2f(s - m_new);
-  l_mine = l_mine * alpha + p;
-  m_mine = m_new;
-  pb[lane] = p;
-#pragma unroll
-  for (int g = 0; g < G; ++g) {
-    const float ag = __shfl_sync(FULL, alpha, g);
-    if (ag != 1.f) {
-#pragma unroll
-      for (int e = 0; e < EPT; ++e) acc[g][e] *= ag;
-    }
-  }
-  __syncwarp();
+}
+
+template <typename T, int D, int G, int TG, bool CHECK>
+__device__ __forceinline__ void decode_pv(const T* __restrict__ vh, int row_elems, int nvalid, const float* pb,
+                                          float (&acc)[G][D / 32]) {
+  constexpr int EPT = D / 32;
 #pragma unroll
   for (int i = 0; i < TG; ++i) {
-    if (i < nvalid) {
+    if (!CHECK || i < nvalid) {
       float vf[EPT];
-      load_vec<T, EPT>(Vs + ((size_t)(t0 + i) * Hkv + h) * D + lane * EPT, vf);
+      load_vec<T, EPT>(vh + i * row_elems, vf);
       float pg[G];
       load_p<G>(pb, i, pg);
 #pragma unroll
@@ -184,12 +163,79 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ Ks, const T* 
         for (int e = 0; e < EPT; ++e) acc[g][e] = fmaf(pg[g], vf[e], acc[g][e]);
     }
   }
+}
+
+// One group of TG tokens (nvalid of them real) for one kv head.
+//
+// The V = TG*G partial sums (each lane holds D/32 features of every one) are
+// reduced with log2(V) transposing butterfly steps -- at each step a lane
+// keeps the half of its remaining values selected by its lane bit and adds
+// the partner's copy of that half -- followed by 5 - log2(V) plain xor steps.
+// Lane l then holds the full score of value j = l >> REM, i.e. of token
+// j / G and query head j % G (lanes differing only in the low REM bits hold
+// the same value). Softmax statistics stay per lane; the probabilities go to
+// a per-warp shared slot for the PV loop.
+template <typename T, int D, int G, int TG>
+__device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* __restrict__ vh, int row_elems,
+                                             int nvalid, int lane, const float (&qv)[G][D / 32],
+                                             float (&acc)[G][D / 32], float& m_mine, float& l_mine, float* pb) {
+  constexpr int EPT = D / 32;
+  constexpr int V = TG * G;
+  static_assert(V <= 32 && (V & (V - 1)) == 0, "group must hold at most 32 power-of-two values");
+  constexpr int K = ilog2c(V);
+  constexpr int REM = 5 - K;
+  constexpr int LG = ilog2c(G);
+  constexpr unsigned FULL = 0xffffffffu;
+  (void)EPT;
+  float v[V];
+  if (nvalid == TG) decode_qk<T, D, G, TG, false>(kh, row_elems, nvalid, qv, v);
+  else decode_qk<T, D, G, TG, true>(kh, row_elems, nvalid, qv, v);
+#pragma unroll
+  for (int st = 0; st < K; ++st) {
+    const int off = 16 >> st;
+    const int half = V >> (st + 1);
+    const bool upper = (lane & off) != 0;
+#pragma unroll
+    for (int j = 0; j < half; ++j) {
+      const float lo = v[j], hi = v[j + half];
+      const float send = upper ? lo : hi;
+      const float keep = upper ? hi : lo;
+      v[j] = keep + __shfl_xor_sync(FULL, send, off);
+    }
+  }
+#pragma unroll
+  for (int off = (1 << REM) >> 1; off >= 1; off >>= 1) v[0] += __shfl_xor_sync(FULL, v[0], off);
+  const int my_tok = lane >> (REM + LG);
+  const float s = (my_tok < nvalid) ? v[0] : kNegInf;
+  float mt = s;
+#pragma unroll
+  for (int off = 1 << (REM + LG); off < 32; off <<= 1) mt = fmaxf(mt, __shfl_xor_sync(FULL, mt, off));
+  const float m_new = fmaxf(m_mine, mt);
+  const float alpha = (m_mine == m_new) ? 1.f : exp2f(m_mine - m_new);
+  const float p = (s == kNegInf) ? 0.f : exp2f(s - m_new);
+  l_mine = l_mine * alpha + p;
+  m_mine = m_new;
+  if ((lane & ((1 << REM) - 1)) == 0) pb[lane >> REM] = p;
+#pragma unroll
+  for (int g = 0; g < G; ++g) {
+    const float ag = __shfl_sync(FULL, alpha, g << REM);
+    if (ag != 1.f) {
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) acc[g][e] *= ag;
+    }
+  }
+  __syncwarp();
+  if (nvalid == TG) decode_pv<T, D, G, TG, false>(vh, row_elems, nvalid, pb, acc);
+  else decode_pv<T, D, G, TG, true>(vh, row_elems, nvalid, pb, acc);
   __syncwarp();
 }
 
-template <typename T, int D, int G>
-__global__ void __launch_bounds__(288, 1) decode_kernel(const DecodeArgs a) {
+template <typename T, int D, int G, int NCW>
+__global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeArgs a) {
   constexpr int EPT = D / 32;
+  constexpr int TG = decode_tg<G>();
+  constexpr int REM = 5 - ilog2c(TG * G);
+  constexpr int LG = ilog2c(G);
   constexpr unsigned FULL = 0xffffffffu;
   extern __shared__ __align__(128) uint8_t smem[];
   const int G_ = G;
@@ -329,8 +375,11 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const DecodeArgs a) {
       if (ok) {
         const T* Ks = reinterpret_cast<const T*>(smem + (size_t)st * 2u * a.stage_bytes);
         const T* Vs = reinterpret_cast<const T*>(smem + (size_t)st * 2u * a.stage_bytes + a.stage_bytes);
-        for (int t0 = sub * (32 / G); t0 < nt; t0 += a.WPH * (32 / G)) {
-          decode_group<T, D, G>(Ks, Vs, t0, min(32 / G, nt - t0), h, a.Hkv, lane, qv, acc, m_mine, l_mine, pb);
+        const int row_elems = a.Hkv * D;
+        for (int t0 = sub * TG; t0 < nt; t0 += a.WPH * TG) {
+          const size_t off = ((size_t)t0 * a.Hkv + h) * D + lane * EPT;
+          decode_group<T, D, G, TG>(Ks + off, Vs + off, row_elems, min(TG, nt - t0), lane, qv, acc, m_mine,
+                                    l_mine, pb);
         }
       }
       __syncwarp();
@@ -340,12 +389,12 @@ __global__ void __launch_bounds__(288, 1) decode_kernel(const DecodeArgs a) {
     // ---- finalize this segment
     float l_red = l_mine;
 #pragma unroll
-    for (int off = G; off < 32; off <<= 1) l_red += __shfl_xor_sync(FULL, l_red, off);
+    for (int off = 1 << (REM + LG); off < 32; off <<= 1) l_red += __shfl_xor_sync(FULL, l_red, off);
     float mg[G], lg[G];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      mg[g] = __shfl_sync(FULL, m_mine, g);
-      lg[g] = __shfl_sync(FULL, l_red, g);
+      mg[g] = __shfl_sync(FULL, m_mine, g << REM);
+      lg[g] = __shfl_sync(FULL, l_red, g << REM);
     }
     if (a.WPH > 1) {
       float* mine = cbuf + (size_t)warp * G * (D + 2);
