@@ -226,7 +226,7 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
             "config": {"workload": "config3: 32 ragged requests, prefix U[0,4096] page-aligned (+1 unaligned), "
                                    "extend U[64,512], 16q/8kv/128, bf16, page 16, RoPE theta 1e6 fused store",
                        "tokens": T, "sum_prefix": int(eb.prefix.sum()), "tile_q_tokens": tile,
-                       "kernel": "extend_tc_kernel (tcgen05)" if tile == 128 // (Hq // Hkv) else "extend_simt_kernel"}}
+                       "kernel": "extend_tc2_kernel (tcgen05, 2 x 128-row tiles)" if tile == 2 * (128 // (Hq // Hkv)) else "extend_simt_kernel"}}
 
 
 # ------------------------------------------------------------------ reference arm
@@ -361,19 +361,42 @@ def run_ours(args):
     dev_kv = torch.empty_like(kv_all)
     meta_bytes = [0]
 
+    h2d = torch.cuda.Stream(device=dev)
+    d2h = torch.cuda.Stream(device=dev)
+
     def e2e_step():
+        """One decode step through the public API with host buffers.
+
+        Layer l's inputs are copied host->device on `h2d` and its output
+        device->host on `d2h`, so the transfers of other layers overlap the
+        attention of layer l. The copies of a step start only after the
+        previous step's compute (no buffer is overwritten while in use).
+        """
+        comp = torch.cuda.current_stream()
         be.prepare_metadata(batch)  # host numpy + plan + one pinned H2D copy
         m = batch.attn_metadata
         meta_bytes[0] = 4 * (m.kv_indptr.numel() + m.kv_indices.numel() + m.kv_last_page_len.numel()
                              + m.cta_indptr.numel() + m.segs.numel() + m.merge_indptr.numel())
-        dev_q.copy_(host_q, non_blocking=True)
-        dev_kv.copy_(host_kv, non_blocking=True)
-        outs = []
+        h2d.wait_stream(comp)
+        ready = []
+        with torch.cuda.stream(h2d):
+            for l in range(Lyr):
+                dev_q[l].copy_(host_q[l], non_blocking=True)
+                dev_kv[l].copy_(host_kv[l], non_blocking=True)
+                ev = torch.cuda.Event()
+                ev.record(h2d)
+                ready.append(ev)
         with ctx.forward_batch(batch):
             for l in range(Lyr):
-                outs.append(layers[l](dev_q[l], dev_kv[l, :, 0], dev_kv[l, :, 1]))
-        for l in range(Lyr):
-            host_out[l].copy_(outs[l], non_blocking=True)
+                comp.wait_event(ready[l])
+                o = layers[l](dev_q[l], dev_kv[l, :, 0], dev_kv[l, :, 1])
+                done = torch.cuda.Event()
+                done.record(comp)
+                d2h.wait_event(done)
+                with torch.cuda.stream(d2h):
+                    host_out[l].copy_(o, non_blocking=True)
+                o.record_stream(d2h)
+        comp.wait_stream(d2h)
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()

@@ -485,7 +485,7 @@ int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* til
   if (plog < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
   const int G = Hq / Hkv;
   if (extend_uses_tc(Hq, Hkv, D, dtype, plog)) {
-    *tile_q = b2a::kTcRows / G;
+    *tile_q = b2a::extend_tc_tile_tokens(G);
   } else {
     if (G > b2a::kSimtRows) return fail(B2A_ERR_UNSUPPORTED, "GQA group %d too large", G);
     *tile_q = b2a::kSimtRows / G;

@@ -4,22 +4,18 @@
 // bottom-right causal). Same contract as extend_simt.cuh; this is the
 // bf16 / head_dim 128 / page_size % 16 == 0 path.
 //
-// CTA = (query tile, kv head h). The 128-row MMA tile packs 128/G query
-// tokens x the G query heads of kv head h (row = token * G + g), so one pass
-// over the K/V of head h serves the whole GQA group.
-//   warp 0     TMA producer: Q tile once (two 64-column SW128 boxes), then K and
-//              V blocks of 128 keys as 16-row boxes, one per 16 keys of a page
-//              (pages are gathered through kv_indices; keys past the sequence
-//              load from an out-of-range coordinate and arrive as zeros).
-//   warp 1     MMA issuer (one thread): S = Q K^T into a double-buffered TMEM
-//              accumulator (kind::f16, M=128 N=128, fp32), then O += P V with
-//              P from shared memory (K-major) and V as an MN-major operand.
-//   warp 2     TMEM allocator (512 columns: S0, S1, O).
-//   warps 4-7  softmax / correction / epilogue: thread t owns TMEM lane t =
-//              tile row t, so row max and row sum need no cross-thread
-//              reduction. The running max is only moved when it grows by more
-//              than 8 (log2 units); otherwise p = 2^(s - m_stale) <= 256 keeps
-//              the accumulation exact in fp32 and O is not rescaled.
+// A 128-row MMA tile packs 128/G query tokens x the G query heads of one kv
+// head (row = token * G + g), so a pass over that head's K/V serves the whole
+// GQA group. A CTA owns two such tiles of one request (see extend_tc2_kernel)
+// and streams the request's K/V once for both: K and V blocks of 128 keys
+// are gathered page by page with 16-row SWIZZLE_128B TMA boxes from a 3-D
+// tensor map over the pool (keys past the sequence use an out-of-range
+// coordinate and arrive as zeros). S and O live in TMEM; the softmax
+// threads own one TMEM lane (= tile row) each, so row max and row sum need
+// no cross-thread reduction, and write P (bf16) back into TMEM for the
+// A-from-TMEM PV MMA. The running max only moves when it grows by more than
+// 8 (log2 units); otherwise p = 2^(s - m_stale) <= 256 keeps the fp32
+// accumulation exact and O is not rescaled.
 // Every mbarrier wait is bounded; a wait that gives up records a watchdog
 // code, the roles unwind, in-flight copies and MMAs are drained (bounded) and
 // TMEM is released before the CTA exits.
@@ -36,7 +32,6 @@ namespace b2a {
 constexpr int kTcRows = 128;      // query rows (tokens x GQA heads) per CTA tile
 constexpr int kTcKeys = 128;      // keys per K/V block
 constexpr int kTcD = 128;         // head_dim handled by this kernel
-constexpr int kTcThreads = 256;   // 8 warps
 constexpr uint32_t kTcTileBytes = 128 * 128 * 2;  // one 128x128 bf16 tile (32 KB)
 constexpr uint32_t kTcHalfBytes = kTcTileBytes / 2;  // one 64-column SW128 half (16 KB)
 
@@ -51,21 +46,6 @@ struct TcArgs {
   int page_log2;
   int Hq, G;
   float qscale;  // scale * log2(e)
-};
-
-// shared-memory map (offsets from a 1024-byte aligned base)
-struct TcSmem {
-  static constexpr uint32_t Q = 0;
-  static constexpr uint32_t K0 = Q + kTcTileBytes;
-  static constexpr uint32_t V0 = K0 + 2 * kTcTileBytes;
-  static constexpr uint32_t P = V0 + 2 * kTcTileBytes;
-  static constexpr uint32_t BARS = P + kTcTileBytes;
-  // barriers: q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], s_empty[2], p_full, p_empty, o_full
-  static constexpr int NBARS = 16;
-  static constexpr uint32_t TMEM_SLOT = BARS + NBARS * 8;
-  static constexpr uint32_t ABORT = TMEM_SLOT + 8;
-  static constexpr uint32_t TOTAL = ABORT + 8;
-  static constexpr uint32_t ALLOC = TOTAL + 1024;  // slack for aligning the base
 };
 
 // ------------------------------------------------------------ PTX wrappers
@@ -157,33 +137,85 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
   return false;
 }
 
-// ------------------------------------------------------------ kernel
-__global__ void __launch_bounds__(kTcThreads, 1)
-    extend_tc_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                     const __grid_constant__ CUtensorMap vmap, const TcArgs a) {
+// ------------------------------------------------------------ v2: two Q tiles, P in TMEM
+//
+// CTA = (work item of up to 2 x 128/G query tokens, kv head h). Tile 0 holds
+// the first 128/G tokens, tile 1 the rest; both read the same K/V blocks.
+//   warp 0     TMA producer (Q0, Q1 once; K and V blocks through 2-deep rings)
+//   warp 1     MMA issuer: S_t = Q_t K^T (SS, M=128 N=128), O_t += P_t V (A = P
+//              from TMEM, B = V MN-major from shared memory)
+//   warp 2     TMEM allocator: S0 [0,128) S1 [128,256) O0 [256,384) O1 [384,512);
+//              P_t (bf16, 64 columns) is written over the first half of S_t
+//   warps 4-7  softmax of tile 0, warps 8-11 softmax of tile 1 (one thread
+//              per TMEM lane = tile row)
+// MMA issue order per block j: PV0(j), S0(j+1), PV1(j), S1(j+1). tcgen05 MMAs
+// of one thread complete in order and a commit covers every earlier MMA, so
+// s_full[t] for block j+1 also means PV_t(j) has finished: P_t may be
+// overwritten and O_t may be rescaled by the softmax warps of tile t without
+// waiting on anything else, and S_t(j+1) never overwrites a P_t still in use.
+constexpr int kTc2Threads = 384;
+
+struct Tc2Smem {
+  static constexpr uint32_t Q0 = 0;
+  static constexpr uint32_t Q1 = Q0 + kTcTileBytes;
+  static constexpr uint32_t K0 = Q1 + kTcTileBytes;
+  static constexpr uint32_t V0 = K0 + 2 * kTcTileBytes;
+  static constexpr uint32_t BARS = V0 + 2 * kTcTileBytes;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], mma_done
+  static constexpr int NBARS = 14;
+  static constexpr uint32_t TMEM_SLOT = BARS + NBARS * 8;
+  static constexpr uint32_t ABORT = TMEM_SLOT + 8;
+  static constexpr uint32_t TOTAL = ABORT + 8;
+  static constexpr uint32_t ALLOC = TOTAL + 1024;
+};
+
+__device__ __forceinline__ void tc_mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                              uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&p);
+}
+
+__global__ void __launch_bounds__(kTc2Threads, 1)
+    extend_tc2_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
+                      const __grid_constant__ CUtensorMap vmap, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + TcSmem::BARS);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Tc2Smem::BARS);
   uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;   // [2]
-  uint64_t* k_empty = bars + 3;  // [2]
-  uint64_t* v_full = bars + 5;   // [2]
-  uint64_t* v_empty = bars + 7;  // [2]
-  uint64_t* s_full = bars + 9;   // [2]
-  uint64_t* s_empty = bars + 11; // [2]
-  uint64_t* p_full = bars + 13;
-  uint64_t* p_empty = bars + 14;
-  uint64_t* o_full = bars + 15;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + TcSmem::TMEM_SLOT);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + TcSmem::ABORT);
+  uint64_t* k_full = bars + 1;    // [2]
+  uint64_t* k_empty = bars + 3;   // [2]
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]
+  uint64_t* s_full = bars + 9;    // [2] per tile
+  uint64_t* p_full = bars + 11;   // [2] per tile
+  uint64_t* mma_done = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Tc2Smem::TMEM_SLOT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Tc2Smem::ABORT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.G;
+  const int TT = kTcRows / G;  // tokens per tile
   const int4 w = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
   const int r = w.x, tb = w.y;
-  const int h = blockIdx.y;
-  const int G = a.G;
-  const int nq = min(w.z, kTcRows / G);
+  const int nq = min(w.z, 2 * TT);
   if (w.z > nq && threadIdx.x == 0) watchdog_set(kWdTileTooLarge);
+  const int nq_t[2] = {min(nq, TT), max(0, nq - TT)};
+  const int h = blockIdx.y;
   const int P = 1 << a.page_log2;
   const int q0 = a.qo_indptr[r];
   const int Lq = a.qo_indptr[r + 1] - q0;
@@ -191,8 +223,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int npages = a.kv_indptr[r + 1] - pbeg;
   const int Lkv = npages > 0 ? ((npages - 1) << a.page_log2) + (a.kv_last_page_len ? a.kv_last_page_len[r] : P) : 0;
   const int prefix = Lkv - Lq;
-  const int kv_end = min(Lkv, prefix + tb + nq);  // keys visible to the last row of the tile
-  const int nb = (kv_end + kTcKeys - 1) / kTcKeys;
+  // keys visible to the last row of each tile, and the blocks each tile needs
+  int nb_t[2];
+  for (int t = 0; t < 2; ++t) {
+    const int kv_end = nq_t[t] > 0 ? min(Lkv, prefix + tb + t * TT + nq_t[t]) : 0;
+    nb_t[t] = (kv_end + kTcKeys - 1) / kTcKeys;
+  }
+  const int nb = max(nb_t[0], nb_t[1]);
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -202,11 +239,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_empty[i], 128);
+      mbar_init(&p_full[i], 128);
     }
-    mbar_init(p_full, 128);
-    mbar_init(p_empty, 1);
-    mbar_init(o_full, 1);
+    mbar_init(mma_done, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -220,20 +255,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS0 = tmem, tS1 = tmem + 128, tO = tmem + 256;
 
   if (warp == 0) {
     // ---------------------------------------------------------------- producer
     int issued_k = 0, issued_v = 0;
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, kTcTileBytes);
-      tma_load_3d(smem + TcSmem::Q, &qmap, 0, h * G, q0 + tb, q_full);
-      tma_load_3d(smem + TcSmem::Q + kTcHalfBytes, &qmap, 64, h * G, q0 + tb, q_full);
+      mbar_arrive_expect_tx(q_full, 2 * kTcTileBytes);
+      for (int t = 0; t < 2; ++t) {
+        // tile 1 rows past the request (or the tensor) load as zeros / stay unused
+        tma_load_3d(smem + Tc2Smem::Q0 + t * kTcTileBytes, &qmap, 0, h * G, q0 + tb + t * TT, q_full);
+        tma_load_3d(smem + Tc2Smem::Q0 + t * kTcTileBytes + kTcHalfBytes, &qmap, 64, h * G, q0 + tb + t * TT, q_full);
+      }
     }
     for (int j = 0; j < nb; ++j) {
       const int st = j & 1;
       const uint32_t ph = (uint32_t)(j >> 1) & 1u;
-      // lane l < 16: box b = l/2 (keys j*128 + 16b ..), column half l%2
       int z = (int)a.num_slots;  // out of range -> zero fill
       const int b = lane >> 1, half = lane & 1;
       if (lane < 16) {
@@ -250,7 +286,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive_expect_tx(&k_full[st], kTcTileBytes);
       __syncwarp();
       if (lane < 16)
-        tma_load_3d(smem + TcSmem::K0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &kmap, half * 64, h, z,
+        tma_load_3d(smem + Tc2Smem::K0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &kmap, half * 64, h, z,
                     &k_full[st]);
       ++issued_k;
       ok = __all_sync(0xffffffffu, tc_wait(&v_empty[st], ph ^ 1u, abort_flag));
@@ -258,11 +294,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       if (lane == 0) mbar_arrive_expect_tx(&v_full[st], kTcTileBytes);
       __syncwarp();
       if (lane < 16)
-        tma_load_3d(smem + TcSmem::V0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &vmap, half * 64, h, z,
+        tma_load_3d(smem + Tc2Smem::V0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &vmap, half * 64, h, z,
                     &v_full[st]);
       ++issued_v;
     }
-    // drain: our own copies must land before the CTA may exit
     if (lane == 0) {
       mbar_wait(q_full, 0, kWdExtendDrain);
       for (int i = max(0, issued_k - 2); i < issued_k; ++i) mbar_wait(&k_full[i & 1], (uint32_t)(i >> 1) & 1u, kWdExtendDrain);
@@ -273,159 +308,175 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     if (lane == 0) {
       constexpr uint32_t idesc_qk = tc_idesc(false);
       constexpr uint32_t idesc_pv = tc_idesc(true);
-      const uint32_t sQ = smem_u32(smem + TcSmem::Q);
-      const uint32_t sP = smem_u32(smem + TcSmem::P);
       bool ok = tc_wait(q_full, 0, abort_flag);
-      auto issue_pv = [&](int i) -> bool {
-        const int vs = i & 1;
-        if (!tc_wait(p_full, (uint32_t)i & 1u, abort_flag)) return false;
-        if (!tc_wait(&v_full[vs], (uint32_t)(i >> 1) & 1u, abort_flag)) return false;
-        tc_fence_after();
-        const uint32_t sV = smem_u32(smem + TcSmem::V0 + vs * kTcTileBytes);
-#pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t ad = sw128_desc(sP + (kk >> 2) * kTcHalfBytes + (kk & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(sV + kk * 2048, kTcHalfBytes, 1024);
-          tc_mma_f16(tO, ad, bd, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-        }
-        tc_commit(p_empty);
-        tc_commit(&v_empty[vs]);
-        return true;
-      };
-      for (int j = 0; j < nb && ok; ++j) {
-        const int ks = j & 1;
-        const uint32_t kph = (uint32_t)(j >> 1) & 1u;
-        if (!tc_wait(&k_full[ks], kph, abort_flag) || !tc_wait(&s_empty[ks], kph ^ 1u, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t sK = smem_u32(smem + TcSmem::K0 + ks * kTcTileBytes);
-        const uint32_t tS = ks ? tS1 : tS0;
+      auto issue_s = [&](int t, int j) {
+        const uint32_t sQ = smem_u32(smem + Tc2Smem::Q0 + t * kTcTileBytes);
+        const uint32_t sK = smem_u32(smem + Tc2Smem::K0 + (j & 1) * kTcTileBytes);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint64_t ad = sw128_desc(sQ + (kk >> 2) * kTcHalfBytes + (kk & 3) * 32, 16, 1024);
           const uint64_t bd = sw128_desc(sK + (kk >> 2) * kTcHalfBytes + (kk & 3) * 32, 16, 1024);
-          tc_mma_f16(tS, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
+          tc_mma_f16(tmem + t * 128, ad, bd, idesc_qk, kk > 0 ? 1u : 0u);
         }
-        tc_commit(&s_full[ks]);
-        tc_commit(&k_empty[ks]);
-        if (j >= 1 && !issue_pv(j - 1)) {
+        tc_commit(&s_full[t]);
+      };
+      auto issue_pv = [&](int t, int j) {
+        const uint32_t sV = smem_u32(smem + Tc2Smem::V0 + (j & 1) * kTcTileBytes);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t bd = sw128_desc(sV + kk * 2048, kTcHalfBytes, 1024);
+          tc_mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      if (ok && nb > 0) {
+        ok = tc_wait(&k_full[0], 0, abort_flag);
+        if (ok) {
+          tc_fence_after();
+          for (int t = 0; t < 2; ++t)
+            if (nb_t[t] > 0) issue_s(t, 0);
+          tc_commit(&k_empty[0]);
+        }
+      }
+      for (int j = 0; j < nb && ok; ++j) {
+        if (!tc_wait(&v_full[j & 1], (uint32_t)(j >> 1) & 1u, abort_flag)) {
           ok = false;
           break;
         }
+        const bool more = j + 1 < nb;
+        bool k_next = false;
+        for (int t = 0; t < 2 && ok; ++t) {
+          if (j < nb_t[t]) {
+            if (!tc_wait(&p_full[t], (uint32_t)j & 1u, abort_flag)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            issue_pv(t, j);
+          }
+          if (more && j + 1 < nb_t[t]) {
+            if (!k_next) {
+              if (!tc_wait(&k_full[(j + 1) & 1], (uint32_t)((j + 1) >> 1) & 1u, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              k_next = true;
+            }
+            issue_s(t, j + 1);
+          }
+        }
+        if (!ok) break;
+        tc_commit(&v_empty[j & 1]);
+        if (more) tc_commit(&k_empty[(j + 1) & 1]);
       }
-      if (ok && nb > 0) ok = issue_pv(nb - 1);
-      tc_commit(o_full);  // also fires (with whatever O holds) on the abort path, so nobody waits forever
-      // drain: every MMA we issued has completed once o_full has fired
-      mbar_wait(o_full, 0, kWdExtendDrain);
+      // every MMA issued above has completed once mma_done fires (also on the abort path)
+      tc_commit(mma_done);
+      mbar_wait(mma_done, 0, kWdExtendDrain);
     }
   } else if (warp >= 4) {
     // ---------------------------------------------------------------- softmax + epilogue
-    // tcgen05.ld/st are warp-collective (.sync.aligned): every branch around
-    // them below is warp-uniform (decided with __all_sync / __any_sync).
     constexpr unsigned FULL = 0xffffffffu;
-    const int row = threadIdx.x - 128;  // == TMEM lane
+    const int t = (warp - 4) >> 2;  // tile of this warpgroup
+    const int row = (threadIdx.x - 128) & 127;  // TMEM lane = tile row
     const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t tS = tmem + t * 128 + lane_off;
+    const uint32_t tO = tmem + 256 + t * 128 + lane_off;
     const int tok = row / G;
-    const int qpos = prefix + tb + tok;  // absolute position of this row's query token
+    const int qpos = prefix + tb + t * TT + tok;
+    const int lim_abs = min(qpos, Lkv - 1);  // last visible key of this row
     float m = kNegInf, l = 0.f;
-    uint8_t* sP = smem + TcSmem::P;
     bool ok = true;
-    for (int j = 0; j < nb; ++j) {
-      const int sb = j & 1;
-      ok = __all_sync(FULL, tc_wait(&s_full[sb], (uint32_t)(j >> 1) & 1u, abort_flag));
+    const int my_nb = nb_t[t];
+    for (int j = 0; j < my_nb; ++j) {
+      ok = __all_sync(FULL, tc_wait(&s_full[t], (uint32_t)j & 1u, abort_flag));
       if (!ok) break;
       tc_fence_after();
-      float s[128];
-      {
-        uint32_t u[32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32((sb ? tS1 : tS0) + lane_off + c * 32, u);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) s[c * 32 + i] = __uint_as_float(u[i]);
-        }
-      }
-      tc_fence_before();
-      mbar_arrive(&s_empty[sb]);
-      // scale into the log2 domain and apply the causal / length mask
-      const int kbase = j * kTcKeys;
-      const int limit = min(qpos, Lkv - 1) - kbase;  // keys 0..limit of this block are visible
+      const int limit = lim_abs - j * kTcKeys;  // columns 0..limit are visible
+      const bool full = limit >= kTcKeys - 1;
+      // pass 1: raw row max over the visible columns
       float mx = kNegInf;
-#pragma unroll
-      for (int c = 0; c < 128; ++c) {
-        const float v = (c <= limit) ? s[c] * a.qscale : kNegInf;
-        s[c] = v;
-        mx = fmaxf(mx, v);
-      }
-      const float m_new = fmaxf(m, mx);
-      float alpha = 1.f;
-      if (m == kNegInf) {
-        m = m_new;  // first visible keys: nothing accumulated yet
-      } else if (m_new - m > 8.f) {
-        alpha = exp2f(m - m_new);
-        m = m_new;
-      }
-      // P buffer and O are free once PV of the previous block has completed
-      if (j >= 1) {
-        ok = __all_sync(FULL, tc_wait(p_empty, (uint32_t)(j - 1) & 1u, abort_flag));
-        if (!ok) break;
-        tc_fence_after();
-        if (__any_sync(FULL, alpha != 1.f)) {
-          uint32_t u[32];
-#pragma unroll
-          for (int c = 0; c < 4; ++c) {
-            tmem_ld32(tO + lane_off + c * 32, u);
-            tmem_wait_ld();
-#pragma unroll
-            for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
-            tmem_st32(tO + lane_off + c * 32, u);
-          }
-          tmem_wait_st();
-        }
-      }
-      float psum = 0.f;
-#pragma unroll
-      for (int ch = 0; ch < 16; ++ch) {
-        uint32_t pk[4];
-#pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const float p0 = (s[ch * 8 + 2 * e] == kNegInf) ? 0.f : exp2f(s[ch * 8 + 2 * e] - m);
-          const float p1 = (s[ch * 8 + 2 * e + 1] == kNegInf) ? 0.f : exp2f(s[ch * 8 + 2 * e + 1] - m);
-          psum += p0 + p1;
-          __nv_bfloat162 pp = __floats2bfloat162_rn(p0, p1);
-          pk[e] = *reinterpret_cast<uint32_t*>(&pp);
-        }
-        const int half = ch >> 3, c8 = ch & 7;
-        uint8_t* dst = sP + half * kTcHalfBytes + row * 128 + ((c8 ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-      }
-      l = l * alpha + psum;
-      asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-      tc_fence_before();
-      mbar_arrive(p_full);
-    }
-    // ---- epilogue: O / l -> bf16 rows of the output
-    const bool got_o = __all_sync(FULL, mbar_wait(o_full, 0, kWdExtendBar));
-    tc_fence_after();
-    if (ok && got_o) {
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const int g = row - tok * G;
-      __nv_bfloat16* dst = a.out + ((size_t)(q0 + tb + tok) * a.Hq + h * G + g) * kTcD;
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t u[32];
-        tmem_ld32(tO + lane_off + c * 32, u);
+        tmem_ld32(tS + c * 32, u);
+        tmem_wait_ld();
+        if (full) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(u[i]));
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) mx = (c * 32 + i <= limit) ? fmaxf(mx, __uint_as_float(u[i])) : mx;
+        }
+      }
+      const float m_blk = mx * a.qscale;  // scale > 0 keeps the order
+      float alpha = 1.f;
+      if (m == kNegInf) {
+        m = m_blk;
+      } else if (m_blk - m > 8.f) {
+        alpha = ex2_approx(m - m_blk);
+        m = m_blk;
+      }
+      // O_t is stable here: s_full for this block implies PV_t of the previous block finished
+      if (j > 0 && __any_sync(FULL, alpha != 1.f)) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint32_t u[32];
+          tmem_ld32(tO + c * 32, u);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) u[i] = __float_as_uint(__uint_as_float(u[i]) * alpha);
+          tmem_st32(tO + c * 32, u);
+        }
+      }
+      // pass 2: p = 2^(s*scale - m), packed to bf16 pairs over the first 64 columns of S
+      float psum = 0.f;
+      const float nm = -m;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32], pk[16];
+        tmem_ld32(tS + c * 32, u);
+        tmem_wait_ld();
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const int c0 = c * 32 + 2 * i;
+          float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * i]), a.qscale, nm));
+          float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * i + 1]), a.qscale, nm));
+          if (!full) {
+            p0 = (c0 <= limit) ? p0 : 0.f;
+            p1 = (c0 + 1 <= limit) ? p1 : 0.f;
+          }
+          psum += p0 + p1;
+          pk[i] = pack_bf16x2(p0, p1);
+        }
+        // columns [16c, 16c+16) of P: every S column of this chunk was read above
+        asm volatile(
+            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+            "%14, %15, %16};" ::"r"(tS + c * 16),
+            "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7]),
+            "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]), "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
+            : "memory");
+      }
+      tmem_wait_st();
+      l = l * alpha + psum;
+      tc_fence_before();
+      mbar_arrive(&p_full[t]);
+    }
+    // ---- epilogue: O_t / l -> bf16 rows of the output
+    const bool got = __all_sync(FULL, mbar_wait(mma_done, 0, kWdExtendBar));
+    tc_fence_after();
+    if (ok && got && my_nb > 0) {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const int g = row - tok * G;
+      __nv_bfloat16* dst = a.out + ((size_t)(q0 + tb + t * TT + tok) * a.Hq + h * G + g) * kTcD;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t u[32];
+        tmem_ld32(tO + c * 32, u);
         tmem_wait_ld();
         uint32_t pk[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          __nv_bfloat162 pp = __floats2bfloat162_rn(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
-          pk[i] = *reinterpret_cast<uint32_t*>(&pp);
-        }
-        if (tok < nq) {  // rows past the tile's end are computed but never stored
+        for (int i = 0; i < 16; ++i) pk[i] = pack_bf16x2(__uint_as_float(u[2 * i]) * inv, __uint_as_float(u[2 * i + 1]) * inv);
+        if (tok < nq_t[t]) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i) d4[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
@@ -442,6 +493,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 }
 
 // ------------------------------------------------------------ host side
+// Query tokens per work item of the tcgen05 path: two 128-row tiles.
+inline int extend_tc_tile_tokens(int G) { return 2 * (kTcRows / G); }
+
 inline bool extend_tc_supported(int Hq, int Hkv, int D, int dtype) {
   const int G = Hkv > 0 ? Hq / Hkv : 0;
   return dtype == 1 /* bf16 */ && D == kTcD && (G == 1 || G == 2 || G == 4 || G == 8);
@@ -509,16 +563,16 @@ inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_poo
   a.Hq = Hq;
   a.G = G;
   a.qscale = scale * kLog2e;
-  cudaError_t e = cudaFuncSetAttribute(extend_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)TcSmem::ALLOC);
+  cudaError_t e = cudaFuncSetAttribute(extend_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       (int)Tc2Smem::ALLOC);
   if (e != cudaSuccess) {
     err = std::string("extend_tc: smem attribute: ") + cudaGetErrorString(e);
     return 3;
   }
-  extend_tc_kernel<<<dim3(n_work, Hkv), kTcThreads, TcSmem::ALLOC, st>>>(qm, km, vm, a);
+  extend_tc2_kernel<<<dim3(n_work, Hkv), kTc2Threads, Tc2Smem::ALLOC, st>>>(qm, km, vm, a);
   e = cudaGetLastError();
   if (e != cudaSuccess) {
-    err = std::string("extend_tc_kernel: ") + cudaGetErrorString(e);
+    err = std::string("extend_tc2_kernel: ") + cudaGetErrorString(e);
     return 3;
   }
   err.clear();
