@@ -8,7 +8,7 @@
 #include <string>
 #include <vector>
 
-#include "../../include/b200attn.h"
+#include "b200attn.h"
 #include "common.cuh"
 #include "decode.cuh"
 #include "extend_simt.cuh"

@@ -103,6 +103,16 @@ __device__ __forceinline__ void tmem_st32(uint32_t taddr, const uint32_t (&r)[32
       : "memory");
 }
 
+// 16 consecutive 32-bit columns of this thread's TMEM lane.
+__device__ __forceinline__ void tmem_st16(uint32_t taddr, const uint32_t (&r)[16]) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
+      "%14, %15, %16};" ::"r"(taddr),
+      "r"(r[0]), "r"(r[1]), "r"(r[2]), "r"(r[3]), "r"(r[4]), "r"(r[5]), "r"(r[6]), "r"(r[7]), "r"(r[8]), "r"(r[9]),
+      "r"(r[10]), "r"(r[11]), "r"(r[12]), "r"(r[13]), "r"(r[14]), "r"(r[15])
+      : "memory");
+}
+
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 __device__ __forceinline__ void tmem_wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
@@ -183,6 +193,32 @@ __device__ __forceinline__ float ex2_approx(float x) {
   float y;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
+}
+
+// Packed fp32 pairs (sm_100 FFMA2 / FADD2) and the 3-input max: half the
+// instructions of the scalar forms on the softmax's critical path.
+__device__ __forceinline__ uint64_t f2(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_split(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3f(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
 }
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
@@ -393,21 +429,33 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
       tc_fence_after();
       const int limit = lim_abs - j * kTcKeys;  // columns 0..limit are visible
       const bool full = limit >= kTcKeys - 1;
-      // pass 1: raw row max over the visible columns
-      float mx = kNegInf;
+      // pass 1: raw row max over the visible columns; two TMEM loads per round
+      // trip, 8 independent 3-input max chains
+      float mxs[8];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t u[32];
-        tmem_ld32(tS + c * 32, u);
+      for (int i = 0; i < 8; ++i) mxs[i] = kNegInf;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        uint32_t ua[32], ub[32];
+        tmem_ld32(tS + half * 64, ua);
+        tmem_ld32(tS + half * 64 + 32, ub);
         tmem_wait_ld();
-        if (full) {
+        if (!full) {
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = fmaxf(mx, __uint_as_float(u[i]));
-        } else {
+          for (int i = 0; i < 32; ++i) {
+            if (half * 64 + i > limit) ua[i] = __float_as_uint(kNegInf);
+            if (half * 64 + 32 + i > limit) ub[i] = __float_as_uint(kNegInf);
+          }
+        }
 #pragma unroll
-          for (int i = 0; i < 32; ++i) mx = (c * 32 + i <= limit) ? fmaxf(mx, __uint_as_float(u[i])) : mx;
+        for (int i = 0; i < 32; i += 4) {
+          mxs[(i >> 2) & 7] = max3f(mxs[(i >> 2) & 7], __uint_as_float(ua[i]), __uint_as_float(ua[i + 1]));
+          mxs[(i >> 2) & 7] = max3f(mxs[(i >> 2) & 7], __uint_as_float(ua[i + 2]), __uint_as_float(ua[i + 3]));
+          mxs[(i >> 2) & 7] = max3f(mxs[(i >> 2) & 7], __uint_as_float(ub[i]), __uint_as_float(ub[i + 1]));
+          mxs[(i >> 2) & 7] = max3f(mxs[(i >> 2) & 7], __uint_as_float(ub[i + 2]), __uint_as_float(ub[i + 3]));
         }
       }
+      const float mx = fmaxf(max3f(mxs[0], mxs[1], mxs[2]), fmaxf(max3f(mxs[3], mxs[4], mxs[5]), fmaxf(mxs[6], mxs[7])));
       const float m_blk = mx * a.qscale;  // scale > 0 keeps the order
       float alpha = 1.f;
       if (m == kNegInf) {
@@ -428,35 +476,47 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
           tmem_st32(tO + c * 32, u);
         }
       }
-      // pass 2: p = 2^(s*scale - m), packed to bf16 pairs over the first 64 columns of S
-      float psum = 0.f;
-      const float nm = -m;
+      // pass 2: p = 2^(s*scale - m) (one packed FMA per pair), packed to bf16
+      // pairs over the first 64 columns of S; the next chunk's load is in
+      // flight while a chunk is processed; 4 independent packed row sums.
+      const uint64_t sc2 = f2(a.qscale, a.qscale);
+      const uint64_t nm2 = f2(-m, -m);
+      uint64_t ps2[4] = {f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f), f2(0.f, 0.f)};
+      uint32_t ua[32], ub[32];
+      tmem_ld32(tS, ua);
+      tmem_wait_ld();
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
-        uint32_t u[32], pk[16];
-        tmem_ld32(tS + c * 32, u);
-        tmem_wait_ld();
+        uint32_t(&cur)[32] = (c & 1) ? ub : ua;
+        uint32_t(&nxt)[32] = (c & 1) ? ua : ub;
+        if (c < 3) tmem_ld32(tS + (c + 1) * 32, nxt);
+        uint32_t pk[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
           const int c0 = c * 32 + 2 * i;
-          float p0 = ex2_approx(fmaf(__uint_as_float(u[2 * i]), a.qscale, nm));
-          float p1 = ex2_approx(fmaf(__uint_as_float(u[2 * i + 1]), a.qscale, nm));
+          float x0, x1;
+          f2_split(f2_fma(f2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), sc2, nm2), x0, x1);
+          float p0 = ex2_approx(x0);
+          float p1 = ex2_approx(x1);
           if (!full) {
             p0 = (c0 <= limit) ? p0 : 0.f;
             p1 = (c0 + 1 <= limit) ? p1 : 0.f;
           }
-          psum += p0 + p1;
+          ps2[i & 3] = f2_add(ps2[i & 3], f2(p0, p1));
           pk[i] = pack_bf16x2(p0, p1);
         }
-        // columns [16c, 16c+16) of P: every S column of this chunk was read above
-        asm volatile(
-            "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, "
-            "%14, %15, %16};" ::"r"(tS + c * 16),
-            "r"(pk[0]), "r"(pk[1]), "r"(pk[2]), "r"(pk[3]), "r"(pk[4]), "r"(pk[5]), "r"(pk[6]), "r"(pk[7]),
-            "r"(pk[8]), "r"(pk[9]), "r"(pk[10]), "r"(pk[11]), "r"(pk[12]), "r"(pk[13]), "r"(pk[14]), "r"(pk[15])
-            : "memory");
+        // P columns [16c, 16c+16): every S column below 32(c+1) has been read
+        tmem_st16(tS + c * 16, pk);
+        if (c < 3) tmem_wait_ld();
       }
       tmem_wait_st();
+      float psum;
+      {
+        const uint64_t s01 = f2_add(f2_add(ps2[0], ps2[1]), f2_add(ps2[2], ps2[3]));
+        float lo, hi;
+        f2_split(s01, lo, hi);
+        psum = lo + hi;
+      }
       l = l * alpha + psum;
       tc_fence_before();
       mbar_arrive(&p_full[t]);
