@@ -7,11 +7,14 @@ fused RoPE + KV store of the B new tokens and paged split-KV decode attention
 over the cached context (AttentionLayer.__call__, reference layers.py:103-111).
 
   value  = algorithmic bytes of the step / device time, inputs resident in HBM
-           (each layer's KV working set, ~560 MB, exceeds the 126 MB L2)
+           (each layer's KV working set, ~560 MB, exceeds the 126 MB L2); the
+           28 layers replay as one CUDA graph
   e2e    = the same metric through the public API with HOST buffers: per step
-           prepare_metadata (host numpy + plan + one H2D copy), H2D of every
-           layer's q/k/v from pinned memory, the 28 AttentionLayer calls, and a
-           D2H read of every layer's output
+           the decode metadata is rebuilt on the host (numpy + plan) and copied
+           into the graph's metadata buffers, then one graph replays the H2D
+           of every layer's q/k/v from pinned memory, the 28 AttentionLayer
+           calls and a D2H read of every layer's output (copies of other layers
+           overlap each layer's attention)
   roofline: decode call (decode kernel + split merge) per launch, CUDA events
   cpu_baseline: the CPU oracle port (torch, naive gather + masked SDPA) on one
            layer of the same batch (rank 0, N = 1 only)
@@ -331,9 +334,21 @@ def run_ours(args):
                 else:
                     be.forward(q, k, v, l, batch)
 
-    # ---------------- device-resident timing
+    # ---------------- per-call decode timing for the roofline (eager launches, CUDA events)
     for _ in range(max(args.warmup, 3)):
         step()
+    torch.cuda.synchronize()
+    for _ in range(args.steps):
+        step(record=True)
+    torch.cuda.synchronize()
+    dec_ms = [a.elapsed_time(b) for a, b in dec_events]
+
+    # ---------------- device-resident step: the 28 layers as one CUDA graph
+    g_dev = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_dev):
+        step()
+    for _ in range(max(args.warmup, 3)):
+        g_dev.replay()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
@@ -344,12 +359,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     t0.record()
     for _ in range(args.steps):
-        step(record=True)
+        g_dev.replay()
     t1.record()
     torch.cuda.synchronize()
     clk = clocks.stop()
     ms = t0.elapsed_time(t1) / args.steps
-    dec_ms = [a.elapsed_time(b) for a, b in dec_events]
 
     # ---------------- end to end through the public API with host buffers
     host_q = torch.empty(q_all.shape, dtype=torch.bfloat16, pin_memory=True)
@@ -359,24 +373,17 @@ def run_ours(args):
     host_out = torch.empty((Lyr, B, Hq * D), dtype=torch.bfloat16, pin_memory=True)
     dev_q = torch.empty_like(q_all)
     dev_kv = torch.empty_like(kv_all)
-    meta_bytes = [0]
-
     h2d = torch.cuda.Stream(device=dev)
     d2h = torch.cuda.Stream(device=dev)
 
-    def e2e_step():
-        """One decode step through the public API with host buffers.
+    def e2e_layers():
+        """Copies and attention of one step; captured once as a CUDA graph.
 
-        Layer l's inputs are copied host->device on `h2d` and its output
-        device->host on `d2h`, so the transfers of other layers overlap the
-        attention of layer l. The copies of a step start only after the
-        previous step's compute (no buffer is overwritten while in use).
+        Layer l's inputs go host->device on `h2d` and its output device->host
+        on `d2h`, so the transfers of other layers overlap the attention of
+        layer l (the streams fork from and join the capturing stream).
         """
         comp = torch.cuda.current_stream()
-        be.prepare_metadata(batch)  # host numpy + plan + one pinned H2D copy
-        m = batch.attn_metadata
-        meta_bytes[0] = 4 * (m.kv_indptr.numel() + m.kv_indices.numel() + m.kv_last_page_len.numel()
-                             + m.cta_indptr.numel() + m.segs.numel() + m.merge_indptr.numel())
         h2d.wait_stream(comp)
         ready = []
         with torch.cuda.stream(h2d):
@@ -386,6 +393,7 @@ def run_ours(args):
                 ev = torch.cuda.Event()
                 ev.record(h2d)
                 ready.append(ev)
+        d2h.wait_stream(comp)
         with ctx.forward_batch(batch):
             for l in range(Lyr):
                 comp.wait_event(ready[l])
@@ -395,8 +403,26 @@ def run_ours(args):
                 d2h.wait_event(done)
                 with torch.cuda.stream(d2h):
                     host_out[l].copy_(o, non_blocking=True)
-                o.record_stream(d2h)
         comp.wait_stream(d2h)
+        comp.wait_stream(h2d)
+
+    for _ in range(2):
+        e2e_layers()
+    torch.cuda.synchronize()
+    g_e2e = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g_e2e):
+        e2e_layers()
+    meta = batch.attn_metadata
+    meta_bytes = 4 * (meta.kv_indptr.numel() + meta.kv_indices.numel() + meta.kv_last_page_len.numel()
+                      + meta.cta_indptr.numel() + meta.segs.numel() + meta.merge_indptr.numel())
+    req_rows = np.array([r.table_idx for r in reqs])
+    req_lens = np.array([r.device_len for r in reqs])
+
+    def e2e_step():
+        # prepare_metadata for this step (host numpy + plan + one pinned H2D copy into the
+        # graph's metadata buffers), then the captured copies + 28 attention layers
+        be.refresh_decode_metadata(meta, req_rows, req_lens)
+        g_e2e.replay()
 
     for _ in range(max(args.warmup, 3)):
         e2e_step()
@@ -460,7 +486,7 @@ def run_ours(args):
                 "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_avg, 5), "traffic": None,
             },
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
-                    "h2d_bytes_per_step": int((host_q.numel() + host_kv.numel()) * 2 + meta_bytes[0]),
+                    "h2d_bytes_per_step": int((host_q.numel() + host_kv.numel()) * 2 + meta_bytes),
                     "d2h_bytes_per_step": int(host_out.numel() * 2), "ms_per_step": round(e2e_ms, 4)},
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clk,

@@ -5,6 +5,8 @@
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
+#include <map>
+#include <mutex>
 #include <string>
 #include <vector>
 
@@ -154,11 +156,27 @@ int decode_config(int Hq, int Hkv, int D, size_t es, DecodeCfg& c) {
   return fail(B2A_ERR_UNSUPPORTED, "decode config (Hq %d, Hkv %d, D %d) does not fit in shared memory", Hq, Hkv, D);
 }
 
+// Raises a kernel's dynamic shared-memory limit once per (kernel, device), so
+// steady-state launches (and launches inside CUDA graph capture) make no
+// attribute calls.
+int ensure_smem(const void* kern, size_t smem, const char* what) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, size_t> done;
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(B2A_ERR_CUDA, "%s: no current device", what);
+  std::lock_guard<std::mutex> lock(mu);
+  size_t& have = done[{kern, dev}];
+  if (have >= smem) return B2A_OK;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "%s: set smem attribute: %s", what, cudaGetErrorString(e));
+  have = smem;
+  return B2A_OK;
+}
+
 template <typename T, int D, int G, int NCW>
 int decode_launch(const b2a::DecodeArgs& a, const DecodeCfg& c, int grid, cudaStream_t st) {
   auto kern = b2a::decode_kernel<T, D, G, NCW>;
-  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)c.smem);
-  if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "decode: set smem attribute: %s", cudaGetErrorString(e));
+  if (int rc = ensure_smem((const void*)kern, c.smem, "decode")) return rc;
   kern<<<grid, (c.NCW + 1) * 32, c.smem, st>>>(a);
   return check_launch("decode_kernel");
 }
@@ -549,6 +567,7 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int G = Hq / Hkv;
   if (extend_uses_tc(Hq, Hkv, D, dtype, plog)) {
+    if (int rc = ensure_smem((const void*)b2a::extend_tc2_kernel, b2a::Tc2Smem::ALLOC, "extend_tc")) return rc;
     return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
                                  plog, work, n_work, T, Hq, Hkv, scale, out, st, g_err);
   }
@@ -576,8 +595,7 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
         constexpr int Gc = decltype(gc)::value;
         auto kern = b2a::extend_simt_kernel<Tt, Dc, Gc>;
         const size_t smem = b2a::extend_simt_smem(Dc);
-        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "extend: smem attribute: %s", cudaGetErrorString(e));
+        if (int rc = ensure_smem((const void*)kern, smem, "extend")) return rc;
         kern<<<dim3(n_work, Hkv), b2a::kSimtThreads, smem, st>>>(a);
         return check_launch("extend_simt_kernel");
       });

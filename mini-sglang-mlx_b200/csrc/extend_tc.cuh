@@ -623,14 +623,9 @@ inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_poo
   a.Hq = Hq;
   a.G = G;
   a.qscale = scale * kLog2e;
-  cudaError_t e = cudaFuncSetAttribute(extend_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)Tc2Smem::ALLOC);
-  if (e != cudaSuccess) {
-    err = std::string("extend_tc: smem attribute: ") + cudaGetErrorString(e);
-    return 3;
-  }
+  // the caller has raised the kernel's shared-memory limit (once per device)
   extend_tc2_kernel<<<dim3(n_work, Hkv), kTc2Threads, Tc2Smem::ALLOC, st>>>(qm, km, vm, a);
-  e = cudaGetLastError();
+  cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     err = std::string("extend_tc2_kernel: ") + cudaGetErrorString(e);
     return 3;

@@ -113,6 +113,21 @@ class B200AttnBackend(BaseAttnBackend):
             page_size=P, batch_size=len(lens),
         )
 
+    def refresh_decode_metadata(self, meta: B200DecodeMetadata, rows: np.ndarray, lens: np.ndarray) -> None:
+        """Recompute the decode indices of a batch into ``meta``'s existing device tensors.
+
+        For replaying a CUDA graph captured with ``meta``: the new plan must have the
+        same sizes (same requests and page counts), otherwise ValueError.
+        """
+        P = meta.page_size
+        kv_indptr, kv_indices, lpl = paged_kv_indices(self.page_table, rows, lens, P, check=CHECK_METADATA)
+        cta_indptr, segs, merge_indptr, n_partials = nat.decode_plan(kv_indptr, lpl, P, meta.num_ctas)
+        if n_partials > meta.n_partials:
+            raise ValueError("refresh_decode_metadata: plan needs more split partials than the captured one")
+        self._stager.upload([kv_indptr, kv_indices, lpl, cta_indptr, segs, merge_indptr], self.device,
+                            out=[meta.kv_indptr, meta.kv_indices, meta.kv_last_page_len, meta.cta_indptr,
+                                 meta.segs, meta.merge_indptr])
+
     def forward_decode(self, q: torch.Tensor, layer_id: int, meta: B200DecodeMetadata) -> torch.Tensor:
         B = meta.batch_size
         assert q.shape == (B, self.Hq, self.D), q.shape

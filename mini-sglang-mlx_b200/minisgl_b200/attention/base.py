@@ -79,8 +79,18 @@ class PinnedStager:
 
     ALIGN = 16  # int32 elements: every array starts on a 64-byte boundary (int4 loads on the device)
 
-    def upload(self, arrays: Sequence[np.ndarray], device: torch.device) -> List[torch.Tensor]:
+    def upload(self, arrays: Sequence[np.ndarray], device: torch.device,
+               out: Sequence[torch.Tensor] | None = None) -> List[torch.Tensor]:
+        """Copy int32 host arrays to the device in one transfer.
+
+        With ``out``, the arrays land in those existing device tensors instead
+        (same sizes; a CUDA graph that captured them reads the new values).
+        """
         sizes = [int(a.size) for a in arrays]
+        if out is not None:
+            if [int(t.numel()) for t in out] != sizes:
+                raise ValueError("upload(out=...): array sizes differ from the target tensors")
+            return self._upload_into(arrays, out)
         padded = [(n + self.ALIGN - 1) // self.ALIGN * self.ALIGN for n in sizes]
         total = max(self.ALIGN, sum(padded))
         slot = self._next
@@ -109,6 +119,13 @@ class PinnedStager:
             out.append(dev[off:off + n])
             off += pn
         return out
+
+
+    def _upload_into(self, arrays: Sequence[np.ndarray], out: Sequence[torch.Tensor]) -> List[torch.Tensor]:
+        staged = self.upload(arrays, out[0].device)
+        for dst, src in zip(out, staged):
+            dst.copy_(src.view(dst.shape), non_blocking=True)
+        return list(out)
 
 
 class BaseAttnBackend(ABC):

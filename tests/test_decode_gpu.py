@@ -130,3 +130,37 @@ def test_decode_watchdog_clear():
     code = ctypes.c_int(-1)
     nat.call("b2a_device_error", torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
     assert code.value == 0
+
+
+def test_decode_cuda_graph_replay_with_refreshed_metadata():
+    """The decode path is capturable: launches are stream-ordered and allocation-free.
+
+    A graph captured once replays with new q values (copied into the captured
+    buffer) and metadata rebuilt in place by refresh_decode_metadata.
+    """
+    import torch
+
+    from minisgl_b200.attention import B200AttnBackend
+
+    rng = np.random.default_rng(21)
+    Hq, Hkv, D, P = 16, 8, 128, 16
+    lens = rng.integers(1, 900, size=23)
+    pb = W.allocate_pages(lens, 32768, P, rng)
+    kv, hk, hv = _pool(pb.num_slots, Hkv, D, "bfloat16", rng)
+    be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=P)
+    meta = be.decode_metadata_from_lens(pb.rows, pb.lens)
+    q_buf = to_dev(rand(rng, (len(lens), Hq, D), "bfloat16"), "bfloat16")
+    be.forward_decode(q_buf, 0, meta)  # warm-up outside capture
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        out = be.forward_decode(q_buf, 0, meta)
+    idx, mask = O.naive_prepare_decode(pb.page_table, pb.rows, pb.lens)
+    for trial in range(2):
+        q = rand(rng, (len(lens), Hq, D), "bfloat16")
+        q_buf.copy_(to_dev(q, "bfloat16"))
+        be.refresh_decode_metadata(meta, pb.rows, pb.lens)
+        g.replay()
+        torch.cuda.synchronize()
+        ref = O.naive_forward_decode(q, hk[0], hv[0], idx, mask, D ** -0.5)
+        assert max_abs(to_np(out), ref) <= TOL["bfloat16"], trial
