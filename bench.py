@@ -56,6 +56,7 @@ def parse_args():
     ap.add_argument("--layers", type=int, default=None,
                     help="decode layers per step (default 28 = config 2); fewer only for profiling captures")
     ap.add_argument("--no-extend", action="store_true", help="skip the config-3 extend measurement")
+    ap.add_argument("--no-config5", action="store_true", help="skip the config-5 long-context decode measurement")
     return ap.parse_args()
 
 
@@ -161,6 +162,82 @@ def cpu_sample(lens, page_table, P, Hq, Hkv, D, num_slots, steps, warmup, seed):
     per_call = float(np.mean(times))
     gbs = decode_bytes(lens, P, Hq, Hkv, D, 2) / per_call / 1e9
     return gbs, per_call, torch.get_num_threads()
+
+
+def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
+    """Config 5: request-partitioned long-context decode at Qwen3-8B attention shape.
+
+    1024 sequences, context log-uniform in [1024, 131072] (sum ~27.4 M tokens),
+    32q/8kv/128, bf16, page 16, split-KV. Requests are sharded longest-first
+    across the ranks (no collective); each rank holds ONE layer's pool for its
+    shard (~112 GB at 1 GPU) and times repeated decode calls over it. Every
+    call streams far more than the 126 MB L2, so HBM GB/s is honest. Reported
+    per rank-0 plus the job total (sum of bytes / slowest rank).
+    """
+    import torch
+    import torch.distributed as dist
+
+    from minisgl_b200 import MHAKVCache
+    from minisgl_b200 import workloads as W
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.config import qwen3_8b
+
+    c = W.CONFIG5
+    cfg = qwen3_8b()
+    Hq, Hkv, D, P = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim, c["page_size"]
+    lens_all = W.config5_lens(seed=seed)
+    mine = W.shard_requests(lens_all, world)[rank]
+    lens = lens_all[mine]
+    rng = np.random.default_rng(seed + 7 * rank)
+    pages = int(((lens + P - 1) // P).sum())
+    num_slots = (pages + 64) * P
+    free_bytes, _ = torch.cuda.mem_get_info(dev)
+    need = num_slots * Hkv * D * 2 * 2
+    if need > free_bytes - (8 << 30):
+        return {"skipped": f"pool of {need / 1e9:.1f} GB does not fit next to the bench's buffers"}
+    pb = W.allocate_pages(lens, num_slots, P, rng)
+    kv = MHAKVCache(1, num_slots, Hkv, D, torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(seed + 99 * rank)
+    kv.k[0].normal_(generator=gen)
+    kv.v[0].normal_(generator=gen)
+    be = B200AttnBackend(cfg, kv, pb.page_table, page_size=P)
+    meta = be.decode_metadata_from_lens(pb.rows, pb.lens)
+    q = torch.randn((len(lens), Hq, D), device=dev, generator=gen).to(torch.bfloat16)
+    for _ in range(3):
+        be.forward_decode(q, 0, meta)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    evs = []
+    for _ in range(max(5, min(steps, 20))):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        be.forward_decode(q, 0, meta)
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    nbytes = decode_bytes(pb.lens, P, Hq, Hkv, D, 2)
+    stats = torch.tensor([ms], dtype=torch.float64, device=dev)
+    work = torch.tensor([float(nbytes)], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+        dist.all_reduce(work, op=dist.ReduceOp.SUM)
+    peak, kind = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    out = {"metric": "decode-attn HBM GB/s, one layer call per rank", "value": round(float(work.item()) / (stats.item() * 1e-3) / 1e9, 1),
+           "unit": "GB/s", "scaling": "strong (1024 requests split across ranks)", "ms_per_call_max_rank": round(stats.item(), 4),
+           "rank0": {"requests": int(len(lens)), "sum_ctx_tokens": int(lens.sum()), "bytes_per_call": nbytes,
+                     "ms_per_call": round(ms, 4), "achieved": round(gbs, 1), "frac": round(gbs / peak, 4),
+                     "n_partials": meta.n_partials, "pool_gb": round(need / 1e9, 1)},
+           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                        "frac": round(gbs / peak, 4), "peak_kind": kind},
+           "config": {"workload": "config5: Qwen3-8B attention (32q/8kv/128), bf16, page 16, 1024 seqs, "
+                                  "L log-uniform [1024, 131072], split-KV, request-partitioned",
+                      "sum_ctx_tokens_all": int(lens_all.sum())}}
+    del kv, be, meta, q
+    torch.cuda.empty_cache()
+    return out
 
 
 def extend_flops(prefix: np.ndarray, extend: np.ndarray, Hq: int, D: int) -> float:
@@ -456,6 +533,12 @@ def run_ours(args):
     achieved = dbytes / (dec_avg * 1e-3) / 1e9
     launches_per_step = Lyr * (2 + (1 if meta.n_partials > 0 else 0))
 
+    # free the config-2 pools and graphs before the long-context measurement
+    del g_dev, g_e2e, kv, be, ctx, layers, q_all, kv_all, dev_q, dev_kv
+    set_global_ctx(None)
+    torch.cuda.synchronize()
+    torch.cuda.empty_cache()
+    c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps)
     ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
 
     line = None
@@ -495,6 +578,8 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if ext is not None:
             line["extend_config3"] = ext
+        if c5 is not None:
+            line["decode_config5"] = c5
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -43,13 +43,12 @@ def allocate_pages(lens: np.ndarray, num_slots: int, page_size: int, rng: np.ran
     free = rng.permutation(num_pages).astype(np.int64)
     max_seq_len = max_seq_len or int(need.max(initial=1)) * P
     table = np.zeros((len(lens), max_seq_len), dtype=np.int32)
+    ar = np.arange(P, dtype=np.int64)
     off = 0
-    for b, n in enumerate(need.tolist()):
-        pages = free[off:off + n]
-        off += n
-        slots = (pages[:, None] * P + np.arange(P)[None, :]).reshape(-1)
+    for b, n in enumerate(need.tolist()):  # request b takes the next n pages of the shuffled list
         m = min(n * P, max_seq_len)
-        table[b, :m] = slots[:m]
+        table[b, :m] = (free[off:off + n, None] * P + ar[None, :]).reshape(-1)[:m]
+        off += n
     return PagedBatch(table, np.arange(len(lens), dtype=np.int64), lens, P, num_slots)
 
 

@@ -164,3 +164,32 @@ def test_decode_cuda_graph_replay_with_refreshed_metadata():
         torch.cuda.synchronize()
         ref = O.naive_forward_decode(q, hk[0], hv[0], idx, mask, D ** -0.5)
         assert max_abs(to_np(out), ref) <= TOL["bfloat16"], trial
+
+
+@pytest.mark.parametrize("num_ctas", [None, 37])
+def test_long_context_decode_qwen3_8b_shape(num_ctas):
+    """Config-5 shape (32q/8kv/128, bf16, page 16) with contexts up to 32K tokens,
+    split across many CTAs; oracle: per-request contiguous SDPA (tests/test_attention.py:10-16)."""
+    rng = np.random.default_rng(5)
+    lens = np.array([32768, 20011, 5, 4097])
+    pb = W.allocate_pages(lens, 65536, 16, rng)
+    out, _, meta = _run_backend_decode_ref(pb, 32, 8, 128, "bfloat16", num_ctas)
+    assert meta.n_partials > 0
+    assert out <= TOL["bfloat16"], out
+
+
+def _run_backend_decode_ref(pb, Hq, Hkv, D, dtype, num_ctas):
+    import torch
+
+    from minisgl_b200.attention import B200AttnBackend
+
+    rng = np.random.default_rng(9)
+    kv, hk, hv = _pool(pb.num_slots, Hkv, D, dtype, rng)
+    be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=pb.page_size)
+    meta = be.decode_metadata_from_lens(pb.rows, pb.lens, num_ctas=num_ctas)
+    q = rand(rng, (pb.batch_size, Hq, D), dtype)
+    out = to_np(be.forward_decode(to_dev(q, dtype), 0, meta))
+    torch.cuda.synchronize()
+    per_req = [pb.page_table[b, : int(pb.lens[b])] for b in range(pb.batch_size)]
+    ref = O.reference_decode_per_request(q.astype(np.float32), hk[0], hv[0], per_req, D ** -0.5)
+    return max_abs(out, ref), None, meta
