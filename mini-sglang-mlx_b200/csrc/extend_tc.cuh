@@ -163,6 +163,10 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
 // s_full[t] for block j+1 also means PV_t(j) has finished: P_t may be
 // overwritten and O_t may be rescaled by the softmax warps of tile t without
 // waiting on anything else, and S_t(j+1) never overwrites a P_t still in use.
+// The softmax releases P_t(j) in two halves (keys 0-63, then 64-127; one
+// mbarrier each), so the first four PV MMAs of the tile run while it
+// finishes the block: the S -> softmax -> PV -> S chain of a tile is what
+// bounds this kernel, the tensor pipe itself runs at full rate.
 constexpr int kTc2Threads = 384;
 
 struct Tc2Smem {
@@ -171,8 +175,10 @@ struct Tc2Smem {
   static constexpr uint32_t K0 = Q1 + kTcTileBytes;
   static constexpr uint32_t V0 = K0 + 2 * kTcTileBytes;
   static constexpr uint32_t BARS = V0 + 2 * kTcTileBytes;
-  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], p_full[2], mma_done
-  static constexpr int NBARS = 14;
+  // q_full, k_full[2], k_empty[2], v_full[2], v_empty[2], s_full[2], (2 spare), mma_done,
+  // p_full[2 tiles] x 4 slots (2 halves used): spacing keeps the words the
+  // softmax warps arrive on apart from the s_full words they poll (measured ~1%)
+  static constexpr int NBARS = 22;
   static constexpr uint32_t TMEM_SLOT = BARS + NBARS * 8;
   static constexpr uint32_t ABORT = TMEM_SLOT + 8;
   static constexpr uint32_t TOTAL = ABORT + 8;
@@ -238,7 +244,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
   uint64_t* v_full = bars + 5;    // [2]
   uint64_t* v_empty = bars + 7;   // [2]
   uint64_t* s_full = bars + 9;    // [2] per tile
-  uint64_t* p_full = bars + 11;   // [2] per tile
+  uint64_t* p_full = bars + 14;   // [tile * 4 + half]: P columns of that half written
   uint64_t* mma_done = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Tc2Smem::TMEM_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Tc2Smem::ABORT);
@@ -275,7 +281,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
       mbar_init(&v_full[i], 1);
       mbar_init(&v_empty[i], 1);
       mbar_init(&s_full[i], 1);
-      mbar_init(&p_full[i], 128);
+      for (int c = 0; c < 2; ++c) mbar_init(&p_full[i * 4 + c], 4);  // one arrive per softmax warp
     }
     mbar_init(mma_done, 1);
     *abort_flag = 0;
@@ -356,10 +362,12 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
         }
         tc_commit(&s_full[t]);
       };
-      auto issue_pv = [&](int t, int j) {
+      // PV K-steps 4 half .. 4 half + 3 read the P columns of one half
+      auto issue_pv = [&](int t, int j, int half) {
         const uint32_t sV = smem_u32(smem + Tc2Smem::V0 + (j & 1) * kTcTileBytes);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int q = 0; q < 4; ++q) {
+          const int kk = half * 4 + q;
           const uint64_t bd = sw128_desc(sV + kk * 2048, kTcHalfBytes, 1024);
           tc_mma_f16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bd, idesc_pv, (j > 0 || kk > 0) ? 1u : 0u);
         }
@@ -382,12 +390,15 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
         bool k_next = false;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j < nb_t[t]) {
-            if (!tc_wait(&p_full[t], (uint32_t)j & 1u, abort_flag)) {
-              ok = false;
-              break;
+            for (int half = 0; half < 2 && ok; ++half) {
+              if (!tc_wait(&p_full[t * 4 + half], (uint32_t)j & 1u, abort_flag)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+              issue_pv(t, j, half);
             }
-            tc_fence_after();
-            issue_pv(t, j);
+            if (!ok) break;
           }
           if (more && j + 1 < nb_t[t]) {
             if (!k_next) {
@@ -491,25 +502,32 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
         uint32_t(&nxt)[32] = (c & 1) ? ua : ub;
         if (c < 3) tmem_ld32(tS + (c + 1) * 32, nxt);
         uint32_t pk[16];
+        float xv[32];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          f2_split(f2_fma(f2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), sc2, nm2), xv[2 * i], xv[2 * i + 1]);
+#pragma unroll
+        for (int i = 0; i < 32; ++i) xv[i] = ex2_approx(xv[i]);
+        if (!full) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) xv[i] = (c * 32 + i <= limit) ? xv[i] : 0.f;
+        }
 #pragma unroll
         for (int i = 0; i < 16; ++i) {
-          const int c0 = c * 32 + 2 * i;
-          float x0, x1;
-          f2_split(f2_fma(f2(__uint_as_float(cur[2 * i]), __uint_as_float(cur[2 * i + 1])), sc2, nm2), x0, x1);
-          float p0 = ex2_approx(x0);
-          float p1 = ex2_approx(x1);
-          if (!full) {
-            p0 = (c0 <= limit) ? p0 : 0.f;
-            p1 = (c0 + 1 <= limit) ? p1 : 0.f;
-          }
-          ps2[i & 3] = f2_add(ps2[i & 3], f2(p0, p1));
-          pk[i] = pack_bf16x2(p0, p1);
+          ps2[i & 3] = f2_add(ps2[i & 3], f2(xv[2 * i], xv[2 * i + 1]));
+          pk[i] = pack_bf16x2(xv[2 * i], xv[2 * i + 1]);
         }
         // P columns [16c, 16c+16): every S column below 32(c+1) has been read
         tmem_st16(tS + c * 16, pk);
+        if (c & 1) {
+          // release this half of P to the PV MMA while the rest is computed
+          tmem_wait_st();
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&p_full[t * 4 + (c >> 1)]);
+        }
         if (c < 3) tmem_wait_ld();
       }
-      tmem_wait_st();
       float psum;
       {
         const uint64_t s01 = f2_add(f2_add(ps2[0], ps2[1]), f2_add(ps2[2], ps2[3]));
@@ -518,8 +536,6 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
         psum = lo + hi;
       }
       l = l * alpha + psum;
-      tc_fence_before();
-      mbar_arrive(&p_full[t]);
     }
     // ---- epilogue: O_t / l -> bf16 rows of the output
     const bool got = __all_sync(FULL, mbar_wait(mma_done, 0, kWdExtendBar));
