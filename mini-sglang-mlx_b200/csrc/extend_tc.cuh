@@ -252,12 +252,12 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.G;
   const int TT = kTcRows / G;  // tokens per tile
-  const int4 w = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
+  const int4 w = reinterpret_cast<const int4*>(a.work)[blockIdx.y];
   const int r = w.x, tb = w.y;
   const int nq = min(w.z, 2 * TT);
   if (w.z > nq && threadIdx.x == 0) watchdog_set(kWdTileTooLarge);
   const int nq_t[2] = {min(nq, TT), max(0, nq - TT)};
-  const int h = blockIdx.y;
+  const int h = blockIdx.x;
   const int P = 1 << a.page_log2;
   const int q0 = a.qo_indptr[r];
   const int Lq = a.qo_indptr[r + 1] - q0;
@@ -639,8 +639,15 @@ inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_poo
   a.Hq = Hq;
   a.G = G;
   a.qscale = scale * kLog2e;
-  // the caller has raised the kernel's shared-memory limit (once per device)
-  extend_tc2_kernel<<<dim3(n_work, Hkv), kTc2Threads, Tc2Smem::ALLOC, st>>>(qm, km, vm, a);
+  // the caller has raised the kernel's shared-memory limit (once per device).
+  // Grid x = kv head, y = work item: the block scheduler hands out the
+  // cost-sorted items with all their heads together, so the most expensive
+  // tiles start first on every head (measured +6% over head-major order);
+  // y is limited to 65535, so longer work lists go out in chunks.
+  for (int off = 0; off < n_work; off += 65535) {
+    a.work = work + 4 * (size_t)off;
+    extend_tc2_kernel<<<dim3(Hkv, std::min(65535, n_work - off)), kTc2Threads, Tc2Smem::ALLOC, st>>>(qm, km, vm, a);
+  }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {
     err = std::string("extend_tc2_kernel: ") + cudaGetErrorString(e);
