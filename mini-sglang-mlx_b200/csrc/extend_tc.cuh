@@ -130,13 +130,13 @@ __device__ __forceinline__ uint64_t sw128_desc(uint32_t saddr, uint32_t lbo_byte
   return d;
 }
 
-// Instruction descriptor, kind::f16: bf16 x bf16 -> fp32, M=128, N=128.
-__host__ __device__ constexpr uint32_t tc_idesc(bool b_mn_major) {
+// Instruction descriptor, kind::f16: bf16 x bf16 -> fp32, M=128, N=n.
+__host__ __device__ constexpr uint32_t tc_idesc(bool b_mn_major, int n = 128) {
   return (1u << 4)                          // D format fp32
          | (1u << 7)                        // A bf16
          | (1u << 10)                       // B bf16
          | ((b_mn_major ? 1u : 0u) << 16)   // B major
-         | ((uint32_t)(128 >> 3) << 17)     // N
+         | ((uint32_t)(n >> 3) << 17)       // N
          | ((uint32_t)(128 >> 4) << 24);    // M
 }
 
