@@ -57,6 +57,7 @@ def parse_args():
                     help="decode layers per step (default 28 = config 2); fewer only for profiling captures")
     ap.add_argument("--no-extend", action="store_true", help="skip the config-3 extend measurement")
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 long-context decode measurement")
+    ap.add_argument("--no-config4", action="store_true", help="skip the config-4 end-to-end offline measurement")
     return ap.parse_args()
 
 
@@ -236,6 +237,74 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
                                   "L log-uniform [1024, 131072], split-KV, request-partitioned",
                       "sum_ctx_tokens_all": int(lens_all.sum())}}
     del kv, be, meta, q
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_e2e_offline(dev, rank: int, world: int, seed: int):
+    """Config 4: end-to-end offline generation through the engine harness (output tok/s).
+
+    Random-init Qwen3-0.6B (bf16), 256 prompts of U[100,1024] random token ids,
+    output U[100,1024] tokens each (ignore_eos, greedy), at most 128 running
+    requests, chunked prefill of 4096 tokens, radix prefix cache, overlap
+    scheduling, page 16, 131072 KV tokens per layer. Wall time around
+    ``LLM.generate`` as benchmark/offline.py:45-48 measures it, after a short
+    warm-up generation. Under torchrun the requests are partitioned (LPT on
+    prompt + output length) and the job throughput is all outputs / slowest rank.
+    """
+    import time
+
+    import torch
+    import torch.distributed as dist
+
+    from minisgl_b200 import workloads as W
+    from minisgl_b200.core import SamplingParams
+    from minisgl_b200.engine import LLM, EngineConfig, qwen3_0_6b_spec
+
+    c = W.CONFIG4
+    prompts_all, outs_all = W.config4_workload(seed=seed)
+    cost = np.array([len(p) for p in prompts_all]) + outs_all
+    mine = W.shard_requests(cost, world)[rank]
+    prompts = [prompts_all[i] for i in mine]
+    outs = [int(outs_all[i]) for i in mine]
+    cfg = EngineConfig(spec=qwen3_0_6b_spec(), dtype="bfloat16", max_running_req=c["max_running_req"],
+                       page_size=c["page_size"], num_tokens=c["num_tokens"], max_extend_tokens=c["max_extend_tokens"])
+    with torch.cuda.device(dev):
+        llm = LLM(cfg, device=dev)
+        rng = np.random.default_rng(seed + 1)
+        llm.generate([rng.integers(0, 10000, 16).astype(np.int32) for _ in range(4)],
+                     SamplingParams(max_tokens=16, ignore_eos=True))
+        llm.num_output_tokens = llm.num_prefill_tokens = llm.num_prefix_hit_tokens = 0
+        llm.num_steps = {"prefill": 0, "decode": 0}
+        torch.cuda.synchronize(dev)
+        if world > 1:
+            dist.barrier()
+        t0 = time.perf_counter()
+        res = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in outs])
+        elapsed = time.perf_counter() - t0
+        assert [len(r["token_ids"]) for r in res] == outs
+        llm.cache.check_integrity()
+        stats = torch.tensor([elapsed], dtype=torch.float64, device=dev)
+        tot = torch.tensor([float(sum(outs))], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(stats, op=dist.ReduceOp.MAX)
+            dist.all_reduce(tot, op=dist.ReduceOp.SUM)
+        out = {"metric": "end-to-end output tok/s (offline, config 4)", "value": round(tot.item() / stats.item(), 1),
+               "unit": "tok/s", "higher_is_better": True, "scaling": "strong (256 requests split across ranks)",
+               "wall_s_max_rank": round(stats.item(), 3),
+               "rank0": {"requests": len(outs), "output_tokens": int(sum(outs)), "wall_s": round(elapsed, 3),
+                         "prefill_tokens": llm.num_prefill_tokens, "prefix_hit_tokens": llm.num_prefix_hit_tokens,
+                         "prefill_steps": llm.num_steps["prefill"], "decode_steps": llm.num_steps["decode"],
+                         "kv_pool_gb": round(llm.engine.kv_cache.nbytes / 1e9, 2),
+                         "model_gb": round(llm.engine.model.nbytes / 1e9, 2)},
+               "config": {"workload": "config4: random-init Qwen3-0.6B bf16, 256 reqs, input/output U[100,1024], "
+                                      "random ids, concurrency 128, greedy, ignore_eos, radix on, overlap on, "
+                                      "chunked prefill 4096, page 16, 131072 KV tokens",
+                          "input_tokens_all": int(sum(len(p) for p in prompts_all)),
+                          "output_tokens_all": int(outs_all.sum())},
+               "data": "synthetic (random token ids, random weights)"}
+        llm.engine.shutdown()
+        del llm
     torch.cuda.empty_cache()
     return out
 
@@ -540,6 +609,7 @@ def run_ours(args):
     torch.cuda.empty_cache()
     c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps)
     ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
+    e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed)
 
     line = None
     if rank == 0:
@@ -580,6 +650,8 @@ def run_ours(args):
             line["extend_config3"] = ext
         if c5 is not None:
             line["decode_config5"] = c5
+        if e2e4 is not None:
+            line["e2e_offline_config4"] = e2e4
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -40,6 +40,7 @@ class B200DecodeMetadata:
     num_ctas: int
     page_size: int
     batch_size: int
+    workspace: torch.Tensor | None = None  # fixed split-partial workspace (CUDA-graph metadata)
 
 
 @dataclass
@@ -128,13 +129,49 @@ class B200AttnBackend(BaseAttnBackend):
                             out=[meta.kv_indptr, meta.kv_indices, meta.kv_last_page_len, meta.cta_indptr,
                                  meta.segs, meta.merge_indptr])
 
+    # ------------------------------------------------------------ decode under CUDA graphs
+    def alloc_decode_graph_metadata(self, batch_size: int, max_pages: int) -> B200DecodeMetadata:
+        """Fixed-capacity decode metadata for a captured decode step of ``batch_size`` requests.
+
+        Every per-step size the kernels need is read on the device (page CSR, the CTA
+        plan, merge ranges), so a captured launch stays valid when
+        ``fill_decode_graph_metadata`` rewrites these buffers in place. The split
+        partials are laid out for the plan's worst case, ``batch_size + num_ctas``
+        (each CTA boundary cuts at most one request), so any later plan fits.
+        """
+        dev, nc = self.device, self.num_ctas
+        cap = batch_size + nc
+        i32 = dict(dtype=torch.int32, device=dev)
+        ws = torch.empty(nat.decode_workspace_bytes(cap, self.Hq, self.D), dtype=torch.uint8, device=dev)
+        return B200DecodeMetadata(
+            kv_indptr=torch.zeros(batch_size + 1, **i32), kv_indices=torch.zeros(max(max_pages, 1), **i32),
+            kv_last_page_len=torch.zeros(batch_size, **i32), cta_indptr=torch.zeros(nc + 1, **i32),
+            segs=torch.zeros((cap + 1, 4), **i32), merge_indptr=torch.zeros(batch_size + 1, **i32),
+            n_partials=cap, num_ctas=nc, page_size=self.page_size, batch_size=batch_size, workspace=ws,
+        )
+
+    def fill_decode_graph_metadata(self, meta: B200DecodeMetadata, rows: np.ndarray, lens: np.ndarray) -> None:
+        """Plan ``len(rows) == meta.batch_size`` requests into ``meta``'s buffers (stream-ordered)."""
+        P = meta.page_size
+        kv_indptr, kv_indices, lpl = paged_kv_indices(self.page_table, rows, lens, P, check=CHECK_METADATA)
+        cta_indptr, segs, merge_indptr, n_partials = nat.decode_plan(kv_indptr, lpl, P, meta.num_ctas)
+        if len(kv_indptr) != meta.batch_size + 1:
+            raise ValueError("fill_decode_graph_metadata: batch size differs from the captured one")
+        if kv_indices.size > meta.kv_indices.numel() or segs.shape[0] > meta.segs.shape[0] or n_partials > meta.n_partials:
+            raise ValueError("fill_decode_graph_metadata: plan exceeds the captured capacity")
+        self._stager.upload(
+            [kv_indptr, kv_indices, lpl, cta_indptr, segs, merge_indptr], self.device,
+            out=[meta.kv_indptr, meta.kv_indices[: kv_indices.size], meta.kv_last_page_len, meta.cta_indptr,
+                 meta.segs[: segs.shape[0]], meta.merge_indptr])
+
     def forward_decode(self, q: torch.Tensor, layer_id: int, meta: B200DecodeMetadata) -> torch.Tensor:
         B = meta.batch_size
         assert q.shape == (B, self.Hq, self.D), q.shape
         q = q.contiguous()
         out = torch.empty_like(q)
         ws_bytes = nat.decode_workspace_bytes(meta.n_partials, self.Hq, self.D)
-        ws = self._workspace_for(ws_bytes)
+        ws = meta.workspace if meta.workspace is not None else self._workspace_for(ws_bytes)
+        assert ws.numel() >= ws_bytes
         nat.call(
             "b2a_decode", q.data_ptr(), self.kv_cache.k_cache(layer_id).data_ptr(),
             self.kv_cache.v_cache(layer_id).data_ptr(), self.kv_cache.num_tokens, meta.kv_indices.data_ptr(),

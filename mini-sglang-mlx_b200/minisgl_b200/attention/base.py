@@ -120,7 +120,6 @@ class PinnedStager:
             off += pn
         return out
 
-
     def _upload_into(self, arrays: Sequence[np.ndarray], out: Sequence[torch.Tensor]) -> List[torch.Tensor]:
         staged = self.upload(arrays, out[0].device)
         for dst, src in zip(out, staged):

@@ -3,10 +3,10 @@
 Mirrors python/minisgl_mlx/core.py:42-158: the three request lengths
 (cached_len / device_len / max_device_len), the per-step Batch fields
 (positions, out_loc, attn_metadata) and the global Context that AttentionLayer
-reads. The scheduler that fills them is out of scope; tests and the bench
-drive these types directly. Tensors here are torch tensors on the GPU
-(positions/out_loc int32 [T]); the page table stays a host numpy array, as in
-the reference.
+reads. Tests and the bench fill them directly; for end-to-end runs the engine
+harness (``minisgl_b200.engine``) is the scheduler that fills them. Tensors
+here are torch tensors on the GPU (positions/out_loc int32 [T]); the page
+table stays a host numpy array, as in the reference.
 """
 
 from __future__ import annotations
@@ -32,6 +32,8 @@ class Req:
     cached_len: int
     output_len: int
     uid: int = 0
+    sampling_params: Any = None  # SamplingParams (engine harness)
+    cache_handle: Any = None  # prefix-cache handle of the matched / inserted prefix
 
     def __post_init__(self) -> None:
         self.device_len = len(self.input_ids)
@@ -46,9 +48,31 @@ class Req:
     def remain_len(self) -> int:
         return self.max_device_len - self.device_len
 
+    @property
+    def can_decode(self) -> bool:
+        return self.remain_len > 0
+
     def complete_one(self) -> None:
         self.cached_len = self.device_len
         self.device_len += 1
+
+    def append_host(self, next_token: int) -> None:
+        self.input_ids = np.append(self.input_ids, np.int32(next_token))
+
+
+@dataclass
+class SamplingParams:
+    """reference core.py:25-39. The engine harness samples greedily (argmax)."""
+
+    temperature: float = 0.0
+    top_k: int = -1
+    top_p: float = 1.0
+    ignore_eos: bool = False
+    max_tokens: int = 1024
+
+    @property
+    def is_greedy(self) -> bool:
+        return (self.temperature <= 0.0 or self.top_k == 1) and self.top_p == 1.0
 
 
 @dataclass
@@ -60,6 +84,7 @@ class Batch:
     input_ids: Any = field(default=None, init=False)
     positions: Any = field(default=None, init=False)  # torch int32 [T] (device)
     out_loc: Any = field(default=None, init=False)  # torch int32 [T] (device)
+    rows: Any = field(default=None, init=False)  # torch int32 [B] page-table rows (engine harness)
     attn_metadata: Any = field(default=None, init=False)
 
     @property

@@ -1,0 +1,107 @@
+"""Random-initialised Qwen3 decoder over packed tokens (the engine harness's model).
+
+Structure of python/minisgl_mlx/models/transformer.py:33-116: per layer an
+RMSNorm, a fused q/k/v projection, per-head q/k RMSNorm (Qwen3), the
+AttentionLayer (fused RoPE + KV store, then the attention backend), the output
+projection, RMSNorm and a fused gate/up SwiGLU MLP, with residuals; a final
+RMSNorm and tied embeddings as the LM head. Prefill keeps only each
+request's last token before the head (``attn_metadata.last_indices``).
+
+Inputs are packed ``[T]`` token ids. GEMMs are cuBLAS through ``F.linear``;
+weights are drawn N(0, 0.02) from a seeded generator (there are no
+checkpoints on this machine), norms start at 1.
+"""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List
+
+import torch
+import torch.nn.functional as F
+
+from ..config import ModelConfig, RotaryConfig
+from ..core import get_global_ctx
+from ..layers import AttentionLayer
+
+
+@dataclass(frozen=True)
+class Qwen3Spec:
+    attn: ModelConfig  # layers, heads, head_dim, rotary
+    hidden_size: int
+    intermediate_size: int
+    vocab_size: int
+    rms_norm_eps: float = 1e-6
+    tie_word_embeddings: bool = True
+
+
+def qwen3_0_6b_spec() -> Qwen3Spec:
+    """Qwen3-0.6B: 28 layers, hidden 1024, FFN 3072, 16 q / 8 kv heads x 128, vocab 151936, tied head."""
+    attn = ModelConfig(28, 16, 8, 128, RotaryConfig(128, 128, 1e6, 40960), hidden_size=1024)
+    return Qwen3Spec(attn, 1024, 3072, 151936)
+
+
+def tiny_spec(num_layers: int = 2, vocab_size: int = 512) -> Qwen3Spec:
+    """A small model of the same structure for parity tests (16 q / 8 kv heads x 128)."""
+    attn = ModelConfig(num_layers, 16, 8, 128, RotaryConfig(128, 128, 1e6, 40960), hidden_size=256)
+    return Qwen3Spec(attn, 256, 512, vocab_size)
+
+
+class _Layer:
+    def __init__(self, spec: Qwen3Spec, layer_id: int, gen: torch.Generator, dtype, device) -> None:
+        a = spec.attn
+        H, D = spec.hidden_size, a.head_dim
+        qkv = (a.num_qo_heads + 2 * a.num_kv_heads) * D
+
+        def w(o, i):
+            return (torch.randn((o, i), generator=gen, device=device, dtype=torch.float32) * 0.02).to(dtype)
+
+        self.in_norm = torch.ones(H, dtype=dtype, device=device)
+        self.qkv = w(qkv, H)
+        self.q_norm = torch.ones(D, dtype=dtype, device=device)
+        self.k_norm = torch.ones(D, dtype=dtype, device=device)
+        self.o = w(H, a.num_qo_heads * D)
+        self.post_norm = torch.ones(H, dtype=dtype, device=device)
+        self.gate_up = w(2 * spec.intermediate_size, H)
+        self.down = w(H, spec.intermediate_size)
+        self.attn = AttentionLayer(layer_id, a.num_qo_heads, a.num_kv_heads, D, a.rotary_config)
+
+
+class Qwen3Model:
+    def __init__(self, spec: Qwen3Spec, dtype: torch.dtype, device: torch.device, seed: int = 42) -> None:
+        self.spec = spec
+        gen = torch.Generator(device=device).manual_seed(seed)
+        self.embed = (torch.randn((spec.vocab_size, spec.hidden_size), generator=gen, device=device,
+                                  dtype=torch.float32) * 0.02).to(dtype)
+        with torch.cuda.device(device):
+            self.layers: List[_Layer] = [_Layer(spec, i, gen, dtype, device) for i in range(spec.attn.num_layers)]
+        self.norm = torch.ones(spec.hidden_size, dtype=dtype, device=device)
+
+    @property
+    def nbytes(self) -> int:
+        ts = [self.embed, self.norm]
+        for L in self.layers:
+            ts += [L.in_norm, L.qkv, L.q_norm, L.k_norm, L.o, L.post_norm, L.gate_up, L.down]
+        return sum(t.numel() * t.element_size() for t in ts)
+
+    def __call__(self, input_ids: torch.Tensor) -> torch.Tensor:
+        """input_ids ``[T]`` -> logits ``[B, vocab]`` of each request's last token."""
+        spec, a = self.spec, self.spec.attn
+        Hq, Hkv, D, eps = a.num_qo_heads, a.num_kv_heads, a.head_dim, spec.rms_norm_eps
+        batch = get_global_ctx().batch
+        h = F.embedding(input_ids, self.embed)
+        T = h.shape[0]
+        for L in self.layers:
+            x = F.rms_norm(h, (spec.hidden_size,), L.in_norm, eps)
+            qkv = F.linear(x, L.qkv)
+            q = F.rms_norm(qkv[:, : Hq * D].view(T, Hq, D), (D,), L.q_norm, eps)
+            k = F.rms_norm(qkv[:, Hq * D: (Hq + Hkv) * D].view(T, Hkv, D), (D,), L.k_norm, eps)
+            v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+            h = h + F.linear(L.attn(q, k, v), L.o)
+            x = F.rms_norm(h, (spec.hidden_size,), L.post_norm, eps)
+            gate, up = F.linear(x, L.gate_up).chunk(2, dim=-1)
+            h = h + F.linear(F.silu(gate) * up, L.down)
+        if batch.is_prefill:
+            h = h[batch.attn_metadata.last_indices.long()]
+        h = F.rms_norm(h, (spec.hidden_size,), self.norm, eps)
+        return F.linear(h, self.embed)

@@ -72,6 +72,8 @@ CONFIG2 = dict(B=128, Hq=16, Hkv=8, D=128, dtype="bfloat16", page_size=16, num_s
 CONFIG3 = dict(B=32, Hq=16, Hkv=8, D=128, dtype="bfloat16", page_size=16, prefix_hi=4096, ext_lo=64,
                ext_hi=512, theta=1e6)
 CONFIG5 = dict(B=1024, Hq=32, Hkv=8, D=128, dtype="bfloat16", page_size=16, lo=1024, hi=131072, layers=36)
+CONFIG4 = dict(num_seqs=256, max_input=1024, max_output=1024, vocab_hi=10000, max_running_req=128,
+               max_extend_tokens=4096, num_tokens=131072, page_size=16)
 
 
 def config1_batch(seed: int = 0) -> PagedBatch:
@@ -121,6 +123,18 @@ def config5_lens(seed: int = 0, batch: int | None = None) -> np.ndarray:
     rng = np.random.default_rng(seed)
     u = rng.uniform(np.log(c["lo"]), np.log(c["hi"]), size=batch or c["B"])
     return np.floor(np.exp(u)).astype(np.int64)
+
+
+def config4_workload(seed: int = 0, num_seqs: int | None = None):
+    """Offline e2e workload (benchmark/offline.py:19-23 shapes): prompts of U[100, 1024] random
+    token ids in [0, 10000], output lengths U[100, 1024]. Returns (prompts, out_lens)."""
+    c = CONFIG4
+    rng = np.random.default_rng(seed)
+    n = num_seqs or c["num_seqs"]
+    prompts = [rng.integers(0, c["vocab_hi"] + 1, int(rng.integers(100, c["max_input"] + 1))).astype(np.int32)
+               for _ in range(n)]
+    out_lens = rng.integers(100, c["max_output"] + 1, n).astype(np.int64)
+    return prompts, out_lens
 
 
 def shard_requests(costs: np.ndarray, world: int) -> List[np.ndarray]:
