@@ -276,6 +276,7 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int):
                      SamplingParams(max_tokens=16, ignore_eos=True))
         llm.num_output_tokens = llm.num_prefill_tokens = llm.num_prefix_hit_tokens = 0
         llm.num_steps = {"prefill": 0, "decode": 0}
+        llm.timing = {k: 0.0 for k in llm.timing}
         torch.cuda.synchronize(dev)
         if world > 1:
             dist.barrier()
@@ -289,12 +290,17 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int):
         if world > 1:
             dist.all_reduce(stats, op=dist.ReduceOp.MAX)
             dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        out = {"metric": "end-to-end output tok/s (offline, config 4)", "value": round(tot.item() / stats.item(), 1),
+        tps = tot.item() / stats.item()
+        out = {"metric": "end-to-end output tok/s (offline, config 4)", "value": round(tps, 1),
                "unit": "tok/s", "higher_is_better": True, "scaling": "strong (256 requests split across ranks)",
+               # the reference's published figure for this workload shape (README.md:84, Apple M5 Ultra,
+               # Metal attention + overlap, real weights, temperature 0.6)
+               "vs_published": {"value": 4427.0, "hardware": "Apple M5 Ultra (Metal)", "ratio": round(tps / 4427.0, 2)},
                "wall_s_max_rank": round(stats.item(), 3),
                "rank0": {"requests": len(outs), "output_tokens": int(sum(outs)), "wall_s": round(elapsed, 3),
                          "prefill_tokens": llm.num_prefill_tokens, "prefix_hit_tokens": llm.num_prefix_hit_tokens,
                          "prefill_steps": llm.num_steps["prefill"], "decode_steps": llm.num_steps["decode"],
+                         "time_s": {k: round(v, 3) for k, v in llm.timing.items()},
                          "kv_pool_gb": round(llm.engine.kv_cache.nbytes / 1e9, 2),
                          "model_gb": round(llm.engine.model.nbytes / 1e9, 2)},
                "config": {"workload": "config4: random-init Qwen3-0.6B bf16, 256 reqs, input/output U[100,1024], "

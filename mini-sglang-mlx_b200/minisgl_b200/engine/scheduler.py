@@ -21,6 +21,7 @@ between two steps.
 
 from __future__ import annotations
 
+import time
 from dataclasses import dataclass
 from typing import Dict, List, Sequence, Tuple
 
@@ -100,6 +101,7 @@ class _Step:
     batch: Batch
     host_tokens: torch.Tensor  # pinned int32 [B]
     done: torch.cuda.Event
+    start: torch.cuda.Event
 
 
 class Scheduler:
@@ -121,6 +123,10 @@ class Scheduler:
         self.num_prefill_tokens = 0
         self.num_prefix_hit_tokens = 0  # prompt tokens served from the prefix cache
         self.num_steps = {"prefill": 0, "decode": 0}
+        # seconds: host scheduling + input/metadata preparation + launches, host result
+        # processing, host blocked on the GPU; GPU time of each phase (events around each step)
+        self.timing = {"host_launch": 0.0, "host_process": 0.0, "host_wait": 0.0, "gpu_prefill": 0.0,
+                       "gpu_decode": 0.0}
         self.graphs = None
         if cfg.cuda_graph_max_bs > 0:
             self.graphs = DecodeGraphs(self.engine, self.table.token_pool, self.engine.pad_row, self.engine.pad_slot,
@@ -159,6 +165,8 @@ class Scheduler:
         self.engine.attn_backend.prepare_metadata(batch)
 
     def _forward(self, batch: Batch) -> _Step:
+        start = torch.cuda.Event(enable_timing=True)
+        start.record()
         gi = getattr(batch, "graph_inputs", None)
         if gi is not None:
             tokens = self.graphs.run(*gi)
@@ -172,15 +180,19 @@ class Scheduler:
         host = self._host_ring[self._ring_next][: batch.size]
         self._ring_next = (self._ring_next + 1) % len(self._host_ring)
         host.copy_(tokens, non_blocking=True)
-        ev = torch.cuda.Event()
+        ev = torch.cuda.Event(enable_timing=True)
         ev.record()
         self.decode.filter_reqs(batch.reqs)
-        return _Step(batch, host, ev)
+        return _Step(batch, host, ev, start)
 
     def _process(self, step: _Step | None) -> None:
         if step is None:
             return
+        t0 = time.perf_counter()
         step.done.synchronize()
+        t1 = time.perf_counter()
+        self.timing["host_wait"] += t1 - t0
+        self.timing["gpu_" + step.batch.phase] += step.start.elapsed_time(step.done) * 1e-3
         tokens = step.host_tokens.tolist()
         new_finished = set()
         with self.cache.lazy_free_region():
@@ -203,6 +215,7 @@ class Scheduler:
                 elif step.batch.is_prefill:
                     self.cache.cache_req(req, finished=False)  # the prompt's KV joins the prefix cache
         self.finished_reqs = new_finished
+        self.timing["host_process"] += time.perf_counter() - t1
 
     def on_token(self, req: Req, token: int, finished: bool) -> None:
         """Called for every sampled token in order (the offline front end collects them)."""
@@ -210,8 +223,10 @@ class Scheduler:
     # ------------------------------------------------------------ loops
     def overlap_step(self, last: _Step | None) -> _Step | None:
         """Launch step t+1 while step t runs, then process step t."""
+        t0 = time.perf_counter()
         batch = self._schedule_next_batch()
         ongoing = self._forward(batch) if batch is not None else None
+        self.timing["host_launch"] += time.perf_counter() - t0
         self._process(last)
         return ongoing
 
