@@ -94,6 +94,28 @@ int b2a_rope_store(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride,
                    void* stream);
 
 /* ------------------------------------------------------------------------
+ * b2a_rope_store with the per-head q/k RMSNorm of Qwen3 fused in front.
+ * No single reference function: it merges the q_norm / k_norm calls of
+ * Attention.__call__ (python/minisgl_mlx/models/transformer.py:54-56, MLX
+ * nn.RMSNorm over head_dim) into the call b2a_rope_store replaces.
+ * Each q (k) head row x of D elements becomes
+ *   y = x * 1 / sqrt(mean(x^2) + norm_eps) * w,  w = q_norm_w (k_norm_w),
+ * rounded to `dtype`, then rotated and stored exactly as b2a_rope_store.
+ * q_norm_w / k_norm_w: device arrays of D elements of `dtype`; either may be
+ * NULL (that kind is not normalised). q_out: NULL (q is normalised and
+ * rotated in place), or a contiguous [T, Hq, D] destination for the final q
+ * rows, in which case q's rows are scratch (e.g. q is a strided view of a
+ * fused qkv projection and q_out feeds the attention call directly).
+ * With q_out, q_norm_w and k_norm_w all NULL this is b2a_rope_store.
+ * ------------------------------------------------------------------------ */
+int b2a_qknorm_rope_store(void* q, int64_t q_row_stride, void* q_out, void* k, int64_t k_row_stride, const void* v,
+                          int64_t v_row_stride, const void* q_norm_w, const void* k_norm_w,
+                          float norm_eps, const int32_t* positions, const int32_t* out_loc,
+                          void* k_pool, void* v_pool, int64_t num_slots, const float* inv_freq,
+                          float rope_scale, int rot_dim, int T, int Hq, int Hkv, int D, int dtype,
+                          void* stream);
+
+/* ------------------------------------------------------------------------
  * Paged decode attention, drop-in form.
  * Same inputs and meaning as paged_decode_attention
  * (python/minisgl_mlx/attention/metal.py:112-131): one query row per request,

@@ -214,7 +214,23 @@ int b2a_rope_store(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride,
                    int64_t v_row_stride, const int32_t* positions, const int32_t* out_loc, void* k_pool,
                    void* v_pool, int64_t num_slots, const float* inv_freq, float rope_scale, int rot_dim, int T,
                    int Hq, int Hkv, int D, int dtype, void* stream) {
+  return b2a_qknorm_rope_store(q, q_row_stride, nullptr, k, k_row_stride, v, v_row_stride, nullptr, nullptr, 0.f,
+                               positions, out_loc, k_pool, v_pool, num_slots, inv_freq, rope_scale, rot_dim, T, Hq,
+                               Hkv, D, dtype, stream);
+}
+
+int b2a_qknorm_rope_store(void* q, int64_t q_row_stride, void* q_out, void* k, int64_t k_row_stride, const void* v,
+                          int64_t v_row_stride, const void* q_norm_w, const void* k_norm_w, float norm_eps,
+                          const int32_t* positions, const int32_t* out_loc, void* k_pool, void* v_pool,
+                          int64_t num_slots, const float* inv_freq, float rope_scale, int rot_dim, int T, int Hq,
+                          int Hkv, int D, int dtype, void* stream) {
   if (T < 0) return fail(B2A_ERR_INVALID, "T must be >= 0");
+  const size_t es = dtype_size(dtype);
+  if ((q_norm_w || k_norm_w) && !(norm_eps >= 0.f)) return fail(B2A_ERR_INVALID, "norm_eps must be >= 0");
+  if ((q_norm_w || q_out) && Hq > 0 && !q) return fail(B2A_ERR_INVALID, "q_norm_w / q_out given without q");
+  if (es && ((q_norm_w && !aligned(q_norm_w, es)) || (k_norm_w && !aligned(k_norm_w, es)) ||
+             (q_out && !aligned(q_out, es))))
+    return fail(B2A_ERR_INVALID, "norm weights and q_out must be aligned to their element size");
   if (T == 0) return ok();
   if (Hq < 0 || Hkv <= 0 || D <= 0) return fail(B2A_ERR_INVALID, "bad head shape");
   if (rot_dim < 0 || rot_dim > D || (rot_dim & 1)) return fail(B2A_ERR_INVALID, "rot_dim %d invalid for D %d", rot_dim, D);
@@ -223,12 +239,13 @@ int b2a_rope_store(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride,
   if (store && (!k_pool || !v_pool || !out_loc || !v)) return fail(B2A_ERR_INVALID, "store needs k_pool, v_pool, v, out_loc");
   if (store && num_slots <= 0) return fail(B2A_ERR_INVALID, "num_slots must be > 0");
   if (rotate && (!positions || !inv_freq)) return fail(B2A_ERR_INVALID, "rope needs positions and inv_freq");
-  if (!k || (rotate && Hq > 0 && !q)) return fail(B2A_ERR_INVALID, "q/k pointers are NULL");
+  if (!k || ((rotate || q_norm_w) && Hq > 0 && !q)) return fail(B2A_ERR_INVALID, "q/k pointers are NULL");
   if (q_row_stride < (int64_t)Hq * D || k_row_stride < (int64_t)Hkv * D || (store && v_row_stride < (int64_t)Hkv * D))
     return fail(B2A_ERR_INVALID, "row strides smaller than a token row");
   b2a::RopeStoreArgs a;
   a.q = q;
   a.q_stride = q_row_stride;
+  a.q_out = q_out;
   a.k = k;
   a.k_stride = k_row_stride;
   a.v = v;
@@ -238,11 +255,14 @@ int b2a_rope_store(void* q, int64_t q_row_stride, void* k, int64_t k_row_stride,
   a.k_pool = store ? k_pool : nullptr;
   a.v_pool = store ? v_pool : nullptr;
   a.inv_freq = inv_freq;
+  a.q_norm_w = q_norm_w;
+  a.k_norm_w = k_norm_w;
+  a.norm_eps = norm_eps;
   a.rope_scale = rope_scale;
   a.rot_dim = rot_dim;
   a.num_slots = num_slots;
   a.T = T;
-  a.Hq = rotate ? Hq : 0;  // q rows only matter when rotating
+  a.Hq = (rotate || q_norm_w || q_out) ? Hq : 0;  // q rows matter when rotated, normalised or moved
   a.Hkv = Hkv;
   a.D = D;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);

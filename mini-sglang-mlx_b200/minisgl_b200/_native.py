@@ -46,6 +46,11 @@ SIGNATURES = {
         [_P, c_int64, _P, c_int64, _P, c_int64, _P, _P, _P, _P, c_int64, _P, c_float, c_int,
          c_int, c_int, c_int, c_int, c_int, _P],
     ),
+    "b2a_qknorm_rope_store": (
+        c_int,
+        [_P, c_int64, _P, _P, c_int64, _P, c_int64, _P, _P, c_float, _P, _P, _P, _P, c_int64, _P, c_float, c_int,
+         c_int, c_int, c_int, c_int, c_int, _P],
+    ),
     "b2a_paged_decode": (
         c_int,
         [_P, _P, _P, c_int64, _P, _P, c_int, c_int, c_int, c_int, c_float, _P, c_int, _P],

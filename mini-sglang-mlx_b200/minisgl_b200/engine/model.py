@@ -1,8 +1,9 @@
 """Random-initialised Qwen3 decoder over packed tokens (the engine harness's model).
 
 Structure of python/minisgl_mlx/models/transformer.py:33-116: per layer an
-RMSNorm, a fused q/k/v projection, per-head q/k RMSNorm (Qwen3), the
-AttentionLayer (fused RoPE + KV store, then the attention backend), the output
+RMSNorm, a fused q/k/v projection, per-head q/k RMSNorm (Qwen3; fused into
+the AttentionLayer's RoPE + KV-store kernel), the AttentionLayer (then the
+attention backend), the output
 projection, RMSNorm and a fused gate/up SwiGLU MLP, with residuals; a final
 RMSNorm and tied embeddings as the LM head. Prefill keeps only each
 request's last token before the head (``attn_metadata.last_indices``).
@@ -94,10 +95,11 @@ class Qwen3Model:
         for L in self.layers:
             x = F.rms_norm(h, (spec.hidden_size,), L.in_norm, eps)
             qkv = F.linear(x, L.qkv)
-            q = F.rms_norm(qkv[:, : Hq * D].view(T, Hq, D), (D,), L.q_norm, eps)
-            k = F.rms_norm(qkv[:, Hq * D: (Hq + Hkv) * D].view(T, Hkv, D), (D,), L.k_norm, eps)
+            q = qkv[:, : Hq * D].view(T, Hq, D)
+            k = qkv[:, Hq * D: (Hq + Hkv) * D].view(T, Hkv, D)
             v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
-            h = h + F.linear(L.attn(q, k, v), L.o)
+            # q/k RMSNorm fused into the RoPE + KV-store kernel
+            h = h + F.linear(L.attn(q, k, v, L.q_norm, L.k_norm, eps), L.o)
             x = F.rms_norm(h, (spec.hidden_size,), L.post_norm, eps)
             gate, up = F.linear(x, L.gate_up).chunk(2, dim=-1)
             h = h + F.linear(F.silu(gate) * up, L.down)

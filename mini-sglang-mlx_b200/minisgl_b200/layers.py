@@ -85,16 +85,28 @@ class RotaryEmbedding:
         return y
 
     def rope_store_(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, positions: torch.Tensor,
-                    out_loc: torch.Tensor, kv_cache, layer_id: int) -> None:
-        """Rotate q, k IN PLACE and scatter rotated k and v into ``kv_cache`` layer ``layer_id``."""
+                    out_loc: torch.Tensor, kv_cache, layer_id: int, q_norm_w: torch.Tensor | None = None,
+                    k_norm_w: torch.Tensor | None = None, eps: float = 1e-6,
+                    q_out: torch.Tensor | None = None) -> None:
+        """Rotate q, k IN PLACE and scatter rotated k and v into ``kv_cache`` layer ``layer_id``.
+
+        With ``q_norm_w`` / ``k_norm_w`` the per-head RMSNorm (Qwen3) is applied first,
+        in the same kernel (b2a_qknorm_rope_store). With ``q_out`` ([T, Hq, D],
+        contiguous) the final q rows go there and q's rows are used as scratch.
+        """
         T, Hq, D = q.shape
         Hkv = k.shape[1]
         for name, t in (("q", q), ("k", k), ("v", v)):
             assert t.stride(2) == 1 and t.stride(1) == D, f"{name} rows must be [H, D] contiguous"
         assert positions.dtype == torch.int32 and out_loc.dtype == torch.int32
+        for w in (q_norm_w, k_norm_w):
+            assert w is None or (w.shape == (D,) and w.dtype == q.dtype and w.is_contiguous())
+        assert q_out is None or (q_out.shape == q.shape and q_out.is_contiguous() and q_out.dtype == q.dtype)
         nat.call(
-            "b2a_rope_store", q.data_ptr(), q.stride(0), k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
-            positions.data_ptr(), out_loc.data_ptr(), kv_cache.k_cache(layer_id).data_ptr(),
+            "b2a_qknorm_rope_store", q.data_ptr(), q.stride(0), None if q_out is None else q_out.data_ptr(),
+            k.data_ptr(), k.stride(0), v.data_ptr(), v.stride(0),
+            None if q_norm_w is None else q_norm_w.data_ptr(), None if k_norm_w is None else k_norm_w.data_ptr(),
+            float(eps), positions.data_ptr(), out_loc.data_ptr(), kv_cache.k_cache(layer_id).data_ptr(),
             kv_cache.v_cache(layer_id).data_ptr(), kv_cache.num_tokens, self.inv_freq.data_ptr(),
             float(self.scale), self.dims, T, Hq, Hkv, D, dtype_code(q.dtype), current_stream_ptr(q.device),
         )
@@ -112,11 +124,24 @@ class AttentionLayer:
         self.head_dim = head_dim
         self.rotary = RotaryEmbedding(rotary_config)
 
-    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
-        """q ``[T, Hq, D]``, k/v ``[T, Hkv, D]`` -> o ``[T, Hq * D]``. q and k are rotated in place."""
+    def __call__(self, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, q_norm_w: torch.Tensor | None = None,
+                 k_norm_w: torch.Tensor | None = None, eps: float = 1e-6) -> torch.Tensor:
+        """q ``[T, Hq, D]``, k/v ``[T, Hkv, D]`` -> o ``[T, Hq * D]``. q and k are rotated in place.
+
+        Extension for Qwen3-style models: with ``q_norm_w`` / ``k_norm_w`` the per-head
+        RMSNorm that the model would apply before this call (models/transformer.py:54-56)
+        is fused into the RoPE + store kernel; q may then be a strided view (e.g. of a
+        fused qkv projection) and the rotated q goes to a fresh contiguous tensor.
+        """
         ctx = get_global_ctx()
         batch = ctx.batch
-        q = q if q.is_contiguous() else q.contiguous()
-        self.rotary.rope_store_(q, k, v, batch.positions, batch.out_loc, ctx.kv_cache, self.layer_id)
+        fused = q_norm_w is not None or k_norm_w is not None
+        if fused or not q.is_contiguous():
+            q_out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+            self.rotary.rope_store_(q, k, v, batch.positions, batch.out_loc, ctx.kv_cache, self.layer_id,
+                                    q_norm_w, k_norm_w, eps, q_out=q_out)
+            q = q_out
+        else:
+            self.rotary.rope_store_(q, k, v, batch.positions, batch.out_loc, ctx.kv_cache, self.layer_id)
         o = ctx.attn_backend.forward(q, k, v, self.layer_id, batch)
         return o.reshape(o.shape[0], self.num_qo_heads * self.head_dim)

@@ -121,3 +121,56 @@ def test_rope_standalone_matches_oracle_large_positions():
     y = rope(to_dev(x, "float32"), torch.from_numpy(pos).cuda())
     ref = O.rope(x, pos, 128, rope.inv_freq_host, 0.25, "float32")
     assert max_abs(to_np(y), ref) <= 1e-5
+
+
+def _rms_rows(x: np.ndarray, w: np.ndarray, eps: float, dtype: str) -> np.ndarray:
+    """models/transformer.py:54-56 (nn.RMSNorm over head_dim) in float64, rounded to dtype."""
+    x = x.astype(np.float64)
+    y = x / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + eps) * w.astype(np.float64)
+    return O.round_to(y, dtype)
+
+
+@pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
+@pytest.mark.parametrize("q_out", [False, True])
+def test_qknorm_rope_store(dtype, q_out):
+    """q/k RMSNorm fused in front of RoPE + store: oracle = norm (rounded) then rope."""
+    import torch
+
+    from minisgl_b200.config import RotaryConfig
+    from minisgl_b200.kvcache import MHAKVCache
+    from minisgl_b200.layers import RotaryEmbedding
+
+    T, Hq, Hkv, D, N, eps = 257, 16, 8, 128, 2048, 1e-6
+    rng, qkv, positions, out_loc = _setup(T, Hq, Hkv, D, dtype, N, seed=3)
+    qkv = O.round_to(qkv * 3.0, dtype)  # rows far from unit RMS
+    wq = O.round_to(rng.uniform(0.5, 1.5, D).astype(np.float32), dtype)
+    wk = O.round_to(rng.uniform(0.5, 1.5, D).astype(np.float32), dtype)
+    kv = MHAKVCache(1, N, Hkv, D, torch_dtype(dtype))
+    buf = to_dev(qkv, dtype)
+    q = buf[:, : Hq * D].view(T, Hq, D)
+    k = buf[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+    v = buf[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+    rope = RotaryEmbedding(RotaryConfig(D, D, 1e6, 131072))
+    qo = torch.empty((T, Hq, D), dtype=torch_dtype(dtype), device="cuda") if q_out else None
+    rope.rope_store_(q, k, v, torch.from_numpy(positions).cuda(), torch.from_numpy(out_loc).cuda(), kv, 0,
+                     to_dev(wq, dtype), to_dev(wk, dtype), eps, q_out=qo)
+    torch.cuda.synchronize()
+
+    hq = qkv[:, : Hq * D].reshape(T, Hq, D)
+    hk = qkv[:, Hq * D:(Hq + Hkv) * D].reshape(T, Hkv, D)
+    hv = qkv[:, (Hq + Hkv) * D:].reshape(T, Hkv, D)
+    ref_q = O.rope(_rms_rows(hq, wq, eps, dtype), positions, D, rope.inv_freq_host, 1.0, dtype)
+    ref_k = O.rope(_rms_rows(hk, wk, eps, dtype), positions, D, rope.inv_freq_host, 1.0, dtype)
+    # the normalised rows reach |x| ~ 5, where one bf16 ulp is 2^-5: the bf16 bound scales
+    # with the magnitude (2e-2 relative above 1, the absolute 2e-2 below)
+    tol = 1e-5 if dtype == "float32" else TOL["bfloat16"]
+
+    def rel_err(got, ref):
+        return float(np.max(np.abs(got.astype(np.float64) - ref) / np.maximum(1.0, np.abs(ref))))
+
+    got_q = to_np(qo if q_out else q)
+    assert rel_err(got_q, ref_q) <= tol
+    assert rel_err(to_np(k), ref_k) <= tol
+    # the pool holds exactly the returned k and the untouched v
+    assert np.array_equal(to_np(kv.k[0])[out_loc], to_np(k))
+    assert np.array_equal(to_np(kv.v[0])[out_loc], hv)
