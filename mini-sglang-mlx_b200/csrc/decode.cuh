@@ -122,10 +122,12 @@ __host__ __device__ constexpr int decode_tg() {
 
 constexpr int ilog2c(int x) { return x <= 1 ? 0 : 1 + ilog2c(x >> 1); }
 
-// Partial dot products of TG tokens x G query heads for one kv head.
+// Partial dot products of TG tokens x G query heads for one kv head. q and the
+// accumulators are packed feature pairs (fma.rn.f32x2): a lane's EPT features
+// give EPT/2 packed FMAs per head, the two halves are added at the end.
 template <typename T, int D, int G, int TG, bool CHECK>
 __device__ __forceinline__ void decode_qk(const T* __restrict__ kh, int row_elems, int nvalid,
-                                          const float (&qv)[G][D / 32], float (&v)[TG * G]) {
+                                          const uint64_t (&qv2)[G][D / 64], float (&v)[TG * G]) {
   constexpr int EPT = D / 32;
 #pragma unroll
   for (int i = 0; i < TG; ++i) {
@@ -134,10 +136,12 @@ __device__ __forceinline__ void decode_qk(const T* __restrict__ kh, int row_elem
       load_vec<T, EPT>(kh + i * row_elems, kf);
 #pragma unroll
       for (int g = 0; g < G; ++g) {
-        float s = 0.f;
+        uint64_t s2 = f2(0.f, 0.f);
 #pragma unroll
-        for (int e = 0; e < EPT; ++e) s = fmaf(qv[g][e], kf[e], s);
-        v[i * G + g] = s;
+        for (int e = 0; e < EPT / 2; ++e) s2 = f2_fma(qv2[g][e], f2(kf[2 * e], kf[2 * e + 1]), s2);
+        float lo, hi;
+        f2_split(s2, lo, hi);
+        v[i * G + g] = lo + hi;
       }
     } else {
 #pragma unroll
@@ -148,7 +152,7 @@ __device__ __forceinline__ void decode_qk(const T* __restrict__ kh, int row_elem
 
 template <typename T, int D, int G, int TG, bool CHECK>
 __device__ __forceinline__ void decode_pv(const T* __restrict__ vh, int row_elems, int nvalid, const float* pb,
-                                          float (&acc)[G][D / 32]) {
+                                          uint64_t (&acc2)[G][D / 64]) {
   constexpr int EPT = D / 32;
 #pragma unroll
   for (int i = 0; i < TG; ++i) {
@@ -158,9 +162,11 @@ __device__ __forceinline__ void decode_pv(const T* __restrict__ vh, int row_elem
       float pg[G];
       load_p<G>(pb, i, pg);
 #pragma unroll
-      for (int g = 0; g < G; ++g)
+      for (int g = 0; g < G; ++g) {
+        const uint64_t p2 = f2(pg[g], pg[g]);
 #pragma unroll
-        for (int e = 0; e < EPT; ++e) acc[g][e] = fmaf(pg[g], vf[e], acc[g][e]);
+        for (int e = 0; e < EPT / 2; ++e) acc2[g][e] = f2_fma(p2, f2(vf[2 * e], vf[2 * e + 1]), acc2[g][e]);
+      }
     }
   }
 }
@@ -177,8 +183,8 @@ __device__ __forceinline__ void decode_pv(const T* __restrict__ vh, int row_elem
 // a per-warp shared slot for the PV loop.
 template <typename T, int D, int G, int TG>
 __device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* __restrict__ vh, int row_elems,
-                                             int nvalid, int lane, const float (&qv)[G][D / 32],
-                                             float (&acc)[G][D / 32], float& m_mine, float& l_mine, float* pb) {
+                                             int nvalid, int lane, const uint64_t (&qv)[G][D / 64],
+                                             uint64_t (&acc)[G][D / 64], float& m_mine, float& l_mine, float* pb) {
   constexpr int EPT = D / 32;
   constexpr int V = TG * G;
   static_assert(V <= 32 && (V & (V - 1)) == 0, "group must hold at most 32 power-of-two values");
@@ -220,8 +226,9 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* 
   for (int g = 0; g < G; ++g) {
     const float ag = __shfl_sync(FULL, alpha, g << REM);
     if (ag != 1.f) {
+      const uint64_t a2 = f2(ag, ag);
 #pragma unroll
-      for (int e = 0; e < EPT; ++e) acc[g][e] *= ag;
+      for (int e = 0; e < EPT / 2; ++e) acc[g][e] = f2_mul(acc[g][e], a2);
     }
   }
   __syncwarp();
@@ -354,14 +361,15 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
   for (int si = seg0; si < seg1; ++si) {
     int b, pbeg, ntok, slot;
     decode_get_seg(a, si, b, pbeg, ntok, slot);
-    float qv[G][EPT], acc[G][EPT];
+    uint64_t qv2[G][EPT / 2], acc2[G][EPT / 2];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
-      load_vec<T, EPT>(qbase + ((size_t)b * a.Hq + h * G + g) * D + lane * EPT, qv[g]);
+      float qf[EPT];
+      load_vec<T, EPT>(qbase + ((size_t)b * a.Hq + h * G + g) * D + lane * EPT, qf);
 #pragma unroll
-      for (int e = 0; e < EPT; ++e) {
-        qv[g][e] *= a.qscale;
-        acc[g][e] = 0.f;
+      for (int e = 0; e < EPT / 2; ++e) {
+        qv2[g][e] = f2(qf[2 * e] * a.qscale, qf[2 * e + 1] * a.qscale);
+        acc2[g][e] = f2(0.f, 0.f);
       }
     }
     float m_mine = kNegInf, l_mine = 0.f;
@@ -378,7 +386,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
         const int row_elems = a.Hkv * D;
         for (int t0 = sub * TG; t0 < nt; t0 += a.WPH * TG) {
           const size_t off = ((size_t)t0 * a.Hkv + h) * D + lane * EPT;
-          decode_group<T, D, G, TG>(Ks + off, Vs + off, row_elems, min(TG, nt - t0), lane, qv, acc, m_mine,
+          decode_group<T, D, G, TG>(Ks + off, Vs + off, row_elems, min(TG, nt - t0), lane, qv2, acc2, m_mine,
                                     l_mine, pb);
         }
       }
@@ -387,6 +395,11 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
       ++ctr;
     }
     // ---- finalize this segment
+    float acc[G][EPT];
+#pragma unroll
+    for (int g = 0; g < G; ++g)
+#pragma unroll
+      for (int e = 0; e < EPT / 2; ++e) f2_split(acc2[g][e], acc[g][2 * e], acc[g][2 * e + 1]);
     float l_red = l_mine;
 #pragma unroll
     for (int off = 1 << (REM + LG); off < 32; off <<= 1) l_red += __shfl_xor_sync(FULL, l_red, off);
