@@ -354,9 +354,13 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
         rope.rope_store_(q, knew, vnew, pos_t, loc_t, kv, 0)
         be._forward_prefill(q, None, None, 0, meta)
     torch.cuda.synchronize()
-    evs = []
+    evs, revs = [], []
     for _ in range(steps):
+        r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        r0.record()
         rope.rope_store_(q, knew, vnew, pos_t, loc_t, kv, 0)
+        r1.record()
+        revs.append((r0, r1))
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
         be._forward_prefill(q, None, None, 0, meta)
@@ -364,6 +368,9 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
         evs.append((a, b))
     torch.cuda.synchronize()
     ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+    rope_ms = float(np.mean([a.elapsed_time(b) for a, b in revs]))
+    rope_bytes = rope_store_bytes(T, Hq, Hkv, D, 2)
+    hbm_peak, hbm_kind = measured_peaks()
     flops = extend_flops(eb.prefix, eb.extend, Hq, D)
     peak = 1636.1
     pk = ROOT / "MEASURED_PEAKS.json"
@@ -381,7 +388,13 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
             "config": {"workload": "config3: 32 ragged requests, prefix U[0,4096] page-aligned (+1 unaligned), "
                                    "extend U[64,512], 16q/8kv/128, bf16, page 16, RoPE theta 1e6 fused store",
                        "tokens": T, "sum_prefix": int(eb.prefix.sum()), "tile_q_tokens": tile,
-                       "kernel": "extend_tc2_kernel (tcgen05, 2 x 128-row tiles)" if tile == 2 * (128 // (Hq // Hkv)) else "extend_simt_kernel"}}
+                       "kernel": "extend_tc2_kernel (tcgen05, 2 x 128-row tiles)" if tile == 2 * (128 // (Hq // Hkv)) else "extend_simt_kernel"},
+            # config 3': the fused RoPE + KV store of the same T tokens (HBM-bound)
+            "rope_store_config3p": {"metric": "fused RoPE + KV store HBM GB/s", "value": round(rope_bytes / (rope_ms * 1e-3) / 1e9, 1),
+                                    "unit": "GB/s", "ms_per_call": round(rope_ms, 4), "bytes_per_call": rope_bytes,
+                                    "roofline": {"bound": "hbm", "peak": hbm_peak, "peak_kind": hbm_kind,
+                                                 "frac": round(rope_bytes / (rope_ms * 1e-3) / 1e9 / hbm_peak, 4)},
+                                    "config": {"tokens": T, "heads": f"{Hq}q/{Hkv}kv x {D}", "dtype": "bf16"}}}
 
 
 # ------------------------------------------------------------------ reference arm
