@@ -200,6 +200,21 @@ int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, in
  * and flagged through the watchdog word.
  * ------------------------------------------------------------------------ */
 int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* tile_q);
+
+/* ------------------------------------------------------------------------
+ * Pack requests' KV rows into pages of 16 contiguous slots (no reference
+ * counterpart: it lets b2a_extend run its tcgen05 path for pools whose page
+ * size is below 16, e.g. the reference's default page_size 1).
+ * For request b < B and position p < tok_indptr[b+1] - tok_indptr[b]:
+ *   src = kv_indices[kv_indptr[b] + p / page_size] * page_size + p % page_size
+ *   k_out[out_page_indptr[b] * 16 + p] = k_pool[src]   (whole Hkv x D rows, bytes)
+ *   v_out[...]                        = v_pool[src]
+ * total_tokens = tok_indptr[B]; k_out / v_out hold out_slots rows.
+ * ------------------------------------------------------------------------ */
+int b2a_pack_kv(const void* k_pool, const void* v_pool, int64_t num_slots, const int32_t* kv_indptr,
+                const int32_t* kv_indices, int page_size, const int32_t* tok_indptr,
+                const int32_t* out_page_indptr, int B, int64_t total_tokens, int Hkv, int D, int dtype,
+                void* k_out, void* v_out, int64_t out_slots, void* stream);
 int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
                     const int32_t* kv_last_page_len, int B, int page_size, int tile_q,
                     int32_t* work, int work_capacity, int* n_work);

@@ -15,6 +15,7 @@
 #include "decode.cuh"
 #include "extend_simt.cuh"
 #include "extend_tc.cuh"
+#include "pack_kv.cuh"
 #include "rope_store.cuh"
 
 namespace {
@@ -529,6 +530,45 @@ int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* til
     *tile_q = b2a::kSimtRows / G;
   }
   return ok();
+}
+
+int b2a_pack_kv(const void* k_pool, const void* v_pool, int64_t num_slots, const int32_t* kv_indptr,
+                const int32_t* kv_indices, int page_size, const int32_t* tok_indptr, const int32_t* out_page_indptr,
+                int B, int64_t total_tokens, int Hkv, int D, int dtype, void* k_out, void* v_out, int64_t out_slots,
+                void* stream) {
+  if (B < 0 || total_tokens < 0) return fail(B2A_ERR_INVALID, "negative size");
+  if (B == 0 || total_tokens == 0) return ok();
+  const size_t es = dtype_size(dtype);
+  if (es == 0) return fail(B2A_ERR_UNSUPPORTED, "dtype %d", dtype);
+  if (Hkv <= 0 || D <= 0) return fail(B2A_ERR_INVALID, "bad head shape");
+  const size_t row = (size_t)Hkv * D * es;
+  if (row % 16) return fail(B2A_ERR_INVALID, "token rows of %zu bytes are not a multiple of 16", row);
+  if (!k_pool || !v_pool || !kv_indptr || !kv_indices || !tok_indptr || !out_page_indptr || !k_out || !v_out)
+    return fail(B2A_ERR_INVALID, "NULL pointer argument");
+  if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(k_out, 16) || !aligned(v_out, 16))
+    return fail(B2A_ERR_INVALID, "pools must be 16-byte aligned");
+  const int plog = ilog2_exact(page_size);
+  if (plog < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
+  if (num_slots <= 0 || out_slots <= 0) return fail(B2A_ERR_INVALID, "num_slots/out_slots must be > 0");
+  b2a::PackArgs a;
+  a.k_pool = reinterpret_cast<const uint8_t*>(k_pool);
+  a.v_pool = reinterpret_cast<const uint8_t*>(v_pool);
+  a.num_slots = num_slots;
+  a.kv_indptr = kv_indptr;
+  a.kv_indices = kv_indices;
+  a.page_log2 = plog;
+  a.tok_indptr = tok_indptr;
+  a.out_page_indptr = out_page_indptr;
+  a.B = B;
+  a.total = total_tokens;
+  a.row_vec = (int)(row / 16);
+  a.k_out = reinterpret_cast<uint8_t*>(k_out);
+  a.v_out = reinterpret_cast<uint8_t*>(v_out);
+  a.out_slots = out_slots;
+  const int64_t blocks = (total_tokens + 7) / 8;
+  if (blocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many rows");
+  b2a::pack_kv_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
+  return check_launch("pack_kv_kernel");
 }
 
 int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,

@@ -73,6 +73,10 @@ SIGNATURES = {
          _P, c_int, _P],
     ),
     "b2a_extend_tile_q": (c_int, [c_int, c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
+    "b2a_pack_kv": (
+        c_int,
+        [_P, _P, c_int64, _P, _P, c_int, _P, _P, c_int, c_int64, c_int, c_int, c_int, _P, _P, c_int64, _P],
+    ),
     "b2a_extend_plan": (
         c_int,
         [_P, _P, _P, c_int, c_int, c_int, _P, c_int, ctypes.POINTER(c_int)],

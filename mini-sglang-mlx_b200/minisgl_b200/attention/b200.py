@@ -55,6 +55,21 @@ class B200PrefillMetadata:
     n_work: int
     total_q: int
     page_size: int
+    # set when the pool's page size is below what the tcgen05 extend needs: the
+    # requests' KV rows are packed into 16-slot pages first (b2a_pack_kv) and
+    # kv_indptr / kv_indices / kv_last_page_len above describe that packed pool
+    pack: "PackPlan | None" = None
+
+
+@dataclass
+class PackPlan:
+    src_kv_indptr: torch.Tensor  # int32 [B+1] page CSR of the real pool (device)
+    src_kv_indices: torch.Tensor  # int32 page ids of the real pool (device)
+    src_page_size: int
+    tok_indptr: torch.Tensor  # int32 [B+1] token CSR (device)
+    out_page_indptr: torch.Tensor  # int32 [B+1] first packed page of each request (device)
+    total_tokens: int
+    out_slots: int
 
 
 def _page_size() -> int:
@@ -77,6 +92,7 @@ class B200AttnBackend(BaseAttnBackend):
         self._page_size = page_size
         self._stager = PinnedStager()
         self._workspace = torch.empty(0, dtype=torch.uint8, device=self.device)
+        self._stage: tuple | None = None  # packed K/V staging pools for small-page prefill
         n = nat.ctypes.c_int(0)
         with torch.cuda.device(self.device):
             nat.call("b2a_decode_num_ctas", self.Hq, self.Hkv, self.D, self.dtype_code, nat.ctypes.byref(n))
@@ -196,6 +212,11 @@ class B200AttnBackend(BaseAttnBackend):
         np.cumsum(extend, out=qo_indptr[1:])
         kv_indptr, kv_indices, lpl = paged_kv_indices(self.page_table, rows, lens, P, check=CHECK_METADATA)
         tile_q = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code, P)
+        if P < self.PACK_PAGE:
+            tile16 = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code, self.PACK_PAGE)
+            if tile16 != tile_q:  # the tensor-core kernel takes this shape once pages are 16 slots
+                return self._packed_extend_metadata(qo_indptr, np.asarray(lens, dtype=np.int64), kv_indptr,
+                                                    kv_indices, P, tile16)
         work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
         dev = self._stager.upload([last_indices, qo_indptr, kv_indptr, kv_indices, lpl, work], self.device)
@@ -205,15 +226,68 @@ class B200AttnBackend(BaseAttnBackend):
             total_q=int(qo_indptr[-1]), page_size=P,
         )
 
+    PACK_PAGE = 16
+
+    def _packed_extend_metadata(self, qo_indptr, lens, src_indptr, src_indices, P, tile_q) -> B200PrefillMetadata:
+        """Metadata for extend over a packed pool: request b's Lkv rows at slots
+        out_page_indptr[b] * 16 + [0, Lkv), pages of 16 with identity ids."""
+        Q = self.PACK_PAGE
+        B = len(lens)
+        tok_indptr = np.zeros(B + 1, np.int64)
+        np.cumsum(lens, out=tok_indptr[1:])
+        npages = (lens + Q - 1) // Q
+        out_page_indptr = np.zeros(B + 1, np.int32)
+        np.cumsum(npages, out=out_page_indptr[1:])
+        total_pages = int(out_page_indptr[-1])
+        kv_indices = np.arange(total_pages, dtype=np.int32)
+        lpl = np.where(npages > 0, lens - (npages - 1) * Q, 0).astype(np.int32)
+        work = nat.extend_plan(qo_indptr, out_page_indptr, lpl, Q, tile_q)
+        last_indices = (qo_indptr[1:] - 1).astype(np.int32)
+        if int(tok_indptr[-1]) >= 2 ** 31:
+            raise ValueError("packed extend: more than 2^31 KV rows in one batch")
+        dev = self._stager.upload([last_indices, qo_indptr, out_page_indptr, kv_indices, lpl, work, src_indptr,
+                                   src_indices, tok_indptr.astype(np.int32)], self.device)
+        pack = PackPlan(src_kv_indptr=dev[6], src_kv_indices=dev[7], src_page_size=P, tok_indptr=dev[8],
+                        out_page_indptr=dev[2], total_tokens=int(tok_indptr[-1]), out_slots=max(total_pages * Q, Q))
+        return B200PrefillMetadata(
+            last_indices=dev[0], q_offsets=qo_indptr.tolist(), qo_indptr=dev[1], kv_indptr=dev[2],
+            kv_indices=dev[3], kv_last_page_len=dev[4], work=dev[5].view(-1, 4), n_work=int(work.shape[0]),
+            total_q=int(qo_indptr[-1]), page_size=Q, pack=pack,
+        )
+
+    def _stage_for(self, slots: int):
+        """Packed K/V staging pools of at least ``slots`` rows.
+
+        Zero-initialised and only ever written with K/V rows, like the real pool: the
+        tail of a request's last packed page (rows past its length) is multiplied by
+        a softmax weight of exactly 0, which is only harmless for finite values.
+        """
+        if self._stage is None or self._stage[0].shape[0] < slots:
+            n = max(slots, 0 if self._stage is None else 2 * self._stage[0].shape[0])
+            self._stage = tuple(torch.zeros((n, self.Hkv, self.D), dtype=self.kv_cache.dtype, device=self.device)
+                                for _ in range(2))
+        return self._stage[0][:slots], self._stage[1][:slots]
+
     def _forward_prefill(self, q, k, v, layer_id: int, meta: B200PrefillMetadata) -> torch.Tensor:
         T = meta.total_q
         assert q.shape == (T, self.Hq, self.D), q.shape
         q = q.contiguous()
         out = torch.empty_like(q)
         B = len(meta.q_offsets) - 1
+        k_pool, v_pool = self.kv_cache.k_cache(layer_id), self.kv_cache.v_cache(layer_id)
+        num_slots = self.kv_cache.num_tokens
+        if meta.pack is not None:
+            pk = meta.pack
+            k_st, v_st = self._stage_for(pk.out_slots)
+            nat.call(
+                "b2a_pack_kv", k_pool.data_ptr(), v_pool.data_ptr(), num_slots, pk.src_kv_indptr.data_ptr(),
+                pk.src_kv_indices.data_ptr(), pk.src_page_size, pk.tok_indptr.data_ptr(),
+                pk.out_page_indptr.data_ptr(), B, pk.total_tokens, self.Hkv, self.D, self.dtype_code,
+                k_st.data_ptr(), v_st.data_ptr(), pk.out_slots, current_stream_ptr(self.device),
+            )
+            k_pool, v_pool, num_slots = k_st, v_st, pk.out_slots
         nat.call(
-            "b2a_extend", q.data_ptr(), self.kv_cache.k_cache(layer_id).data_ptr(),
-            self.kv_cache.v_cache(layer_id).data_ptr(), self.kv_cache.num_tokens, meta.qo_indptr.data_ptr(),
+            "b2a_extend", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), num_slots, meta.qo_indptr.data_ptr(),
             meta.kv_indptr.data_ptr(), meta.kv_indices.data_ptr(), meta.kv_last_page_len.data_ptr(),
             meta.page_size, meta.work.data_ptr(), meta.n_work, T, B, self.Hq, self.Hkv, self.D,
             float(self.scale), out.data_ptr(), self.dtype_code, current_stream_ptr(self.device),

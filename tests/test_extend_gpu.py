@@ -86,3 +86,38 @@ def test_extend_single_request_long_prefix_bf16():
     eb = _batch([4000], [512], 16, seed=3)
     out, ref = _run_extend(eb, 16, 8, 128, "bfloat16", seed=5)
     assert max_abs(out, ref) <= TOL["bfloat16"]
+
+
+@pytest.mark.parametrize("P", [1, 2, 8])
+def test_pack_kv_rows_bit_exact(P):
+    """b2a_pack_kv: every request's rows land at out_page_indptr[b] * 16 + p, byte for byte."""
+    import torch
+
+    from minisgl_b200 import _native as nat
+    from minisgl_b200.attention.base import paged_kv_indices
+
+    rng = np.random.default_rng(7)
+    lens = np.array([1, 15, 16, 17, 200, 33])
+    pb = W.allocate_pages(lens, 4096, P, rng)
+    Hkv, D = 8, 128
+    k_pool = torch.randn((4096, Hkv, D), device="cuda").to(torch.bfloat16)
+    v_pool = torch.randn((4096, Hkv, D), device="cuda").to(torch.bfloat16)
+    kv_indptr, kv_indices, _ = paged_kv_indices(pb.page_table, pb.rows, pb.lens, P)
+    tok = np.concatenate([[0], np.cumsum(lens)]).astype(np.int32)
+    npg = (lens + 15) // 16
+    opi = np.concatenate([[0], np.cumsum(npg)]).astype(np.int32)
+    out_slots = int(opi[-1]) * 16
+    k_out = torch.zeros((out_slots, Hkv, D), dtype=torch.bfloat16, device="cuda")
+    v_out = torch.zeros_like(k_out)
+    dev = [torch.from_numpy(x).cuda() for x in (kv_indptr, kv_indices, tok, opi)]
+    nat.call("b2a_pack_kv", k_pool.data_ptr(), v_pool.data_ptr(), 4096, dev[0].data_ptr(), dev[1].data_ptr(), P,
+             dev[2].data_ptr(), dev[3].data_ptr(), len(lens), int(tok[-1]), Hkv, D, nat.B2A_DTYPE_BF16,
+             k_out.data_ptr(), v_out.data_ptr(), out_slots, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    kp, vp, ko, vo = (t.view(torch.int16).cpu().numpy() for t in (k_pool, v_pool, k_out, v_out))
+    for b, L in enumerate(lens.tolist()):
+        src = pb.page_table[b, :L]
+        dst = opi[b] * 16 + np.arange(L)
+        assert np.array_equal(ko[dst], kp[src]) and np.array_equal(vo[dst], vp[src])
+        tail = np.arange(opi[b] * 16 + L, opi[b + 1] * 16)
+        assert not ko[tail].any() and not vo[tail].any()  # rows past the request stay untouched
