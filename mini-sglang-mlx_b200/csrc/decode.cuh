@@ -308,15 +308,40 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
         const int ncopies = one_run ? 1 : ((nt + P - 1) >> a.page_log2);
         int64_t src_slot[2] = {0, 0};
         int rows_of[2] = {0, 0};
+        int64_t pg[2] = {-2, -2};
         bool in_range = true;
 #pragma unroll
         for (int u = 0; u < 2; ++u) {
           const int j = lane + 32 * u;
           if (j < ncopies) {
             const int64_t page = a.kv_indices[pbeg + (tok >> a.page_log2) + j];
+            pg[u] = page;
             src_slot[u] = one_run ? page * P + (tok & (P - 1)) : page * P;
             rows_of[u] = one_run ? nt : min(P, nt - j * P);
             in_range = in_range && page >= 0 && src_slot[u] + rows_of[u] <= a.num_slots;
+          }
+        }
+        // Consecutive page ids are consecutive slots: a run of them becomes ONE
+        // bulk copy issued by the run's first copy, so small pages (page_size 1
+        // from a fresh allocator) do not pay the copy engine's per-copy cost per
+        // page. Only the stage's last page can be partial, so a run's rows are
+        // min(end * P, nt) - j * P. Bytes and the expect_tx count are unchanged.
+        int run_rows[2] = {0, 0};
+        {
+          const int64_t prev0 = __shfl_up_sync(FULL, pg[0], 1);
+          const int64_t last0 = __shfl_sync(FULL, pg[0], 31);
+          const int64_t prev1 = __shfl_up_sync(FULL, pg[1], 1);
+          const bool h0 = lane < ncopies && (lane == 0 || pg[0] != prev0 + 1);
+          const bool h1 = lane + 32 < ncopies && pg[1] != (lane == 0 ? last0 : prev1) + 1;
+          const uint64_t heads = (uint64_t)__ballot_sync(FULL, h0) | ((uint64_t)__ballot_sync(FULL, h1) << 32);
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int j = lane + 32 * u;
+            if (u == 0 ? h0 : h1) {
+              const uint64_t above = j >= 63 ? 0ull : (heads >> (j + 1)) << (j + 1);
+              const int end = above ? __ffsll((long long)above) - 1 : ncopies;
+              run_rows[u] = min(end * P, nt) - j * P;
+            }
           }
         }
         // Bad page ids never reach the copy engine: record the error, skip the
@@ -332,8 +357,8 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
             const int j = lane + 32 * u;
-            if (j < ncopies) {
-              const uint32_t bytes = (uint32_t)rows_of[u] * a.row_bytes;
+            if (run_rows[u] > 0) {
+              const uint32_t bytes = (uint32_t)run_rows[u] * a.row_bytes;
               const size_t doff = (size_t)j * P * rowB;
               bulk_g2s(kdst + doff, kp + src_slot[u] * rowB, bytes, &full[st], pol);
               bulk_g2s(vdst + doff, vp + src_slot[u] * rowB, bytes, &full[st], pol);
