@@ -249,8 +249,9 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int):
     requests, chunked prefill of 4096 tokens, radix prefix cache, overlap
     scheduling, page 16, 131072 KV tokens per layer. Wall time around
     ``LLM.generate`` as benchmark/offline.py:45-48 measures it, after a short
-    warm-up generation. Under torchrun the requests are partitioned (LPT on
-    prompt + output length) and the job throughput is all outputs / slowest rank.
+    warm-up generation. Under torchrun the requests are partitioned by the
+    prefix-affinity router (engine/router.py: first-page groups, placed
+    longest-first) and the job throughput is all outputs / slowest rank.
     """
     import time
 
@@ -261,10 +262,12 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int):
     from minisgl_b200.core import SamplingParams
     from minisgl_b200.engine import LLM, EngineConfig, qwen3_0_6b_spec
 
+    from minisgl_b200.engine.router import route_requests
+
     c = W.CONFIG4
     prompts_all, outs_all = W.config4_workload(seed=seed)
     cost = np.array([len(p) for p in prompts_all]) + outs_all
-    mine = W.shard_requests(cost, world)[rank]
+    mine = route_requests(prompts_all, cost, world, page_size=c["page_size"])[rank]
     prompts = [prompts_all[i] for i in mine]
     outs = [int(outs_all[i]) for i in mine]
     cfg = EngineConfig(spec=qwen3_0_6b_spec(), dtype="bfloat16", max_running_req=c["max_running_req"],

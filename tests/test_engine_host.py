@@ -173,3 +173,38 @@ def test_chunked_prefill_continues_first():
     assert [r.uid for r in b2.reqs] == [0, 1]  # the chunked request continues ahead of the queue
     assert b2.reqs[0].cached_len == 32 and b2.reqs[0].extend_len == 18
     assert not isinstance(b2.reqs[0], ChunkedReq)
+
+
+def test_router_keeps_prefix_groups_and_balances():
+    from minisgl_b200.engine.router import route_requests
+
+    rng = np.random.default_rng(3)
+    sys_prompts = [rng.integers(0, 1000, 64).astype(np.int32) for _ in range(6)]
+    prompts, owner = [], []
+    for i in range(120):
+        g = i % 6
+        prompts.append(np.concatenate([sys_prompts[g], rng.integers(0, 1000, int(rng.integers(5, 200)))]))
+        owner.append(g)
+    for i in range(40):  # unrelated prompts
+        prompts.append(rng.integers(1000, 2000, int(rng.integers(20, 300))).astype(np.int32))
+        owner.append(-1)
+    costs = np.array([len(p) for p in prompts]) + 100
+    ranks = route_requests(prompts, costs, 4, page_size=16)
+    assert sorted(np.concatenate(ranks).tolist()) == list(range(len(prompts)))
+    rank_of = {int(i): r for r, ids in enumerate(ranks) for i in ids}
+    for g in range(6):  # every shared-prefix group sits on one rank
+        assert len({rank_of[i] for i in range(len(prompts)) if owner[i] == g}) == 1
+    load = np.array([costs[ids].sum() for ids in ranks])
+    assert load.max() <= 1.25 * load.mean()
+
+
+def test_router_splits_an_oversized_group():
+    from minisgl_b200.engine.router import route_requests
+
+    common = np.arange(32, dtype=np.int32)
+    prompts = [np.concatenate([common, [i]]).astype(np.int32) for i in range(64)]
+    costs = np.full(64, 10.0)
+    ranks = route_requests(prompts, costs, 4, page_size=16)
+    load = np.array([costs[ids].sum() for ids in ranks])
+    assert load.min() > 0 and load.max() <= 1.1 * load.mean()  # one giant group is still balanced
+    assert route_requests(prompts, costs, 1, 16)[0].tolist() == list(range(64))
