@@ -1,7 +1,7 @@
 #!/usr/bin/env python
 """Benchmark of the B200 attention backend (decode hot path).
 
-Metric: decode-attention HBM GB/s. One step = one decode
+Headline metric: decode-attention HBM GB/s. One step = one decode
 batch of config 2 through all 28 layers of Qwen3-0.6B attention: per layer the
 fused RoPE + KV store of the B new tokens and paged split-KV decode attention
 over the cached context (AttentionLayer.__call__, reference layers.py:103-111).
@@ -18,6 +18,9 @@ over the cached context (AttentionLayer.__call__, reference layers.py:103-111).
   roofline: decode call (decode kernel + split merge) per launch, CUDA events
   cpu_baseline: the CPU oracle port (torch, naive gather + masked SDPA) on one
            layer of the same batch (rank 0, N = 1 only)
+  extend_config3 / decode_config5 / e2e_offline_config4: the other configurations
+           (tcgen05 extend TFLOP/s with the fused RoPE + store's GB/s, long-context
+           decode GB/s, end-to-end output tok/s of the engine harness)
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
 N > 1 is launched by torchrun: every rank runs its own config-2 batch on its
