@@ -51,7 +51,23 @@ __device__ __forceinline__ void ex2poly2(float& a0, float& a1) {
   a1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
+// Two fp32 -> bf16x2 (round to nearest even) with integer ops and a byte
+// permute: no conversion instruction.
+__device__ __forceinline__ uint32_t pack_int(float lo, float hi) {
+  uint32_t a = __float_as_uint(lo), b = __float_as_uint(hi);
+  a += 0x7fffu + ((a >> 16) & 1u);
+  b += 0x7fffu + ((b >> 16) & 1u);
+  return __byte_perm(a, b, 0x7632);
+}
+__device__ __forceinline__ uint32_t pack_cvt(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
 // MODE 0: ex2.f32   1: ex2.bf16x2 (2 results each)   2: packed polynomial   3: 1:1 MUFU / polynomial
+//      4: ex2.f32 + one cvt.rn.bf16x2.f32 per two results (the softmax's P pack)
+//      5: ex2.f32 + one integer pack per two results
 template <int MODE>
 __global__ void rate(float* out, int iters, float seed) {
   float a[8];
@@ -64,6 +80,10 @@ __global__ void rate(float* out, int iters, float seed) {
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       if (MODE == 0) a[i] = ex2f(a[i]) - 1.0f;
+      if (MODE == 4 || MODE == 5) {
+        a[i] = ex2f(a[i]) - 1.0f;
+        if (i & 1) b[i] ^= MODE == 4 ? pack_cvt(a[i - 1], a[i]) : pack_int(a[i - 1], a[i]);
+      }
       if (MODE == 1) b[i] = ex2b(b[i]) ^ 0x80008000u;
       if (MODE == 2 && (i & 1)) {
         ex2poly2(a[i - 1], a[i]);
@@ -117,6 +137,8 @@ int main() {
   rc |= run<1>("ex2.approx.ftz.bf16x2", d, sms, 4096, 2.0);
   rc |= run<2>("packed polynomial", d, sms, 4096, 1.0);
   rc |= run<3>("MUFU:polynomial 1:1", d, sms, 4096, 1.0);
+  rc |= run<4>("ex2 + cvt bf16x2 pack", d, sms, 4096, 1.0);
+  rc |= run<5>("ex2 + integer pack", d, sms, 4096, 1.0);
   cudaError_t e = cudaDeviceSynchronize();
   printf("status %s\n", cudaGetErrorString(e));
   cudaFree(d);

@@ -1,7 +1,9 @@
 """Build (sm_100a) and run the tensor-core and exponential rate microbenchmarks.
 
-These measure the two units that bound the extend kernel's 128-key block:
-tcgen05.mma at the operand shapes it uses, and 2^x on the MUFU and FMA pipes.
+These measure what bounds the extend kernel's 128-key block: tcgen05.mma at
+the operand shapes it uses (and what a wait between MMA groups costs the
+tensor pipe), 2^x on the MUFU and FMA pipes, and the latency of an mbarrier
+wait.
 Needs a B200; building alone (``--build-only``) needs only nvcc.
 """
 
@@ -22,7 +24,7 @@ FLAGS = ["-O3", "-std=c++17", "-gencode", "arch=compute_100a,code=sm_100a", "-li
 def build() -> list[Path]:
     BUILD.mkdir(exist_ok=True)
     out = []
-    for src in ("mma_rate.cu", "exp2_rate.cu"):
+    for src in ("mma_rate.cu", "exp2_rate.cu", "mbar_wait_latency.cu"):
         exe = BUILD / src.replace(".cu", "")
         subprocess.run(["nvcc", *FLAGS, "-I", str(CSRC), "-I", str(INCLUDE), "-o", str(exe), str(HERE / src)],
                        check=True)
