@@ -158,6 +158,45 @@ int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t nu
                void* stream);
 
 /* ------------------------------------------------------------------------
+ * Decode metadata built on the device (stream-ordered, no host work).
+ * Replaces the per-step host build of MetalAttnBackend.prepare_decode
+ * (python/minisgl_mlx/attention/metal.py:145-152) together with the page-table
+ * row lookup of scheduler/scheduler.py:155-158, and b2a_decode_plan: from a
+ * DEVICE copy of the page table and the batch's rows and lengths it writes
+ * everything b2a_decode reads, so a decode step, metadata included, can be
+ * captured in one CUDA graph.
+ *   page_table      : device int32 [table_rows, table_stride], token-granular
+ *                     (entry p * page_size of a row = first slot of page p)
+ *   rows, lens      : device int32 [B] page-table row and token count
+ *   kv_indptr       : out int32 [B + 1]      page CSR
+ *   kv_indices      : out int32 [idx_capacity] page ids (slot / page_size)
+ *   kv_last_page_len: out int32 [B]
+ *   cta_indptr, segs, merge_indptr: out, as from b2a_decode_plan for the same
+ *                     CSR and num_ctas (identical values); seg_capacity must
+ *                     be >= B + num_ctas (the plan's upper bound), segs
+ *                     16-byte aligned
+ *   counts          : out int32 [2] = {segments, split partials}; pass
+ *                     n_partials = B + num_ctas to b2a_decode with a workspace
+ *                     of that capacity (the merge reads merge_indptr on the
+ *                     device)
+ * num_ctas <= 1024. Lengths above table_stride, rows outside the table and
+ * page ids past idx_capacity are skipped and recorded as device error 34
+ * (b2a_device_error); negative or unaligned entries as 32.
+ *
+ * b2a_page_table_scatter writes page_table[rows[i], cols[i]] = values[i] for
+ * i < n (device arrays): the slots a step allocates on the host, applied to
+ * the device copy. Out-of-range (row, col) pairs are skipped (error 34).
+ * ------------------------------------------------------------------------ */
+int b2a_decode_metadata(const int32_t* page_table, int64_t table_rows, int64_t table_stride,
+                        const int32_t* rows, const int32_t* lens, int B, int page_size, int num_ctas,
+                        int32_t* kv_indptr, int32_t* kv_indices, int64_t idx_capacity,
+                        int32_t* kv_last_page_len, int32_t* cta_indptr, int32_t* segs, int seg_capacity,
+                        int32_t* merge_indptr, int32_t* counts, void* stream);
+int b2a_page_table_scatter(int32_t* page_table, int64_t table_rows, int64_t table_stride,
+                           const int32_t* rows, const int32_t* cols, const int32_t* values, int64_t n,
+                           void* stream);
+
+/* ------------------------------------------------------------------------
  * Paged split-KV decode that allocates nothing and takes no workspace.
  * No counterpart in the reference: it is an extra entry point of this
  * library. It is for callers that cannot allocate device memory when decode

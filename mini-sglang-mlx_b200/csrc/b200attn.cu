@@ -16,6 +16,7 @@
 #include "extend_simt.cuh"
 #include "extend_tc.cuh"
 #include "pack_kv.cuh"
+#include "metadata.cuh"
 #include "rope_store.cuh"
 
 namespace {
@@ -342,6 +343,60 @@ int b2a_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, i
   *n_segs = ns;
   *n_partials = np;
   return ok();
+}
+
+int b2a_decode_metadata(const int32_t* page_table, int64_t table_rows, int64_t table_stride, const int32_t* rows,
+                        const int32_t* lens, int B, int page_size, int num_ctas, int32_t* kv_indptr,
+                        int32_t* kv_indices, int64_t idx_capacity, int32_t* kv_last_page_len, int32_t* cta_indptr,
+                        int32_t* segs, int seg_capacity, int32_t* merge_indptr, int32_t* counts, void* stream) {
+  if (B < 0) return fail(B2A_ERR_INVALID, "B must be >= 0");
+  if (num_ctas <= 0 || num_ctas > b2a::kPlanMaxCtas)
+    return fail(B2A_ERR_INVALID, "num_ctas %d out of [1, %d]", num_ctas, b2a::kPlanMaxCtas);
+  const int plog = ilog2_exact(page_size);
+  if (plog < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
+  if (table_rows <= 0 || table_stride <= 0) return fail(B2A_ERR_INVALID, "empty page table");
+  if (!page_table || !kv_indptr || !kv_indices || !kv_last_page_len || !cta_indptr || !segs || !merge_indptr ||
+      !counts || (B > 0 && (!rows || !lens)))
+    return fail(B2A_ERR_INVALID, "NULL metadata argument");
+  if (!aligned(segs, 16)) return fail(B2A_ERR_INVALID, "segs must be 16-byte aligned (written as int4)");
+  if ((int64_t)seg_capacity < (int64_t)B + num_ctas)
+    return fail(B2A_ERR_WORKSPACE, "seg_capacity %d < B + num_ctas = %lld", seg_capacity, (long long)B + num_ctas);
+  b2a::DecodeMetaArgs a;
+  a.page_table = page_table;
+  a.stride = table_stride;
+  a.table_rows = table_rows;
+  a.rows = rows;
+  a.lens = lens;
+  a.B = B;
+  a.page_log2 = plog;
+  a.num_ctas = num_ctas;
+  a.idx_capacity = idx_capacity;
+  a.seg_capacity = seg_capacity;
+  a.kv_indptr = kv_indptr;
+  a.kv_indices = kv_indices;
+  a.last_page_len = kv_last_page_len;
+  a.cta_indptr = cta_indptr;
+  a.segs = segs;
+  a.merge_indptr = merge_indptr;
+  a.counts = counts;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  b2a::decode_plan_kernel<<<1, b2a::kPlanThreads, 0, st>>>(a);
+  if (int rc = check_launch("decode_plan_kernel")) return rc;
+  if (B == 0) return ok();
+  b2a::decode_indices_kernel<<<std::min(B, 65535), 256, 0, st>>>(a);
+  return check_launch("decode_indices_kernel");
+}
+
+int b2a_page_table_scatter(int32_t* page_table, int64_t table_rows, int64_t table_stride, const int32_t* rows,
+                           const int32_t* cols, const int32_t* values, int64_t n, void* stream) {
+  if (n < 0) return fail(B2A_ERR_INVALID, "n must be >= 0");
+  if (n == 0) return ok();
+  if (!page_table || !rows || !cols || !values) return fail(B2A_ERR_INVALID, "NULL scatter argument");
+  if (table_rows <= 0 || table_stride <= 0) return fail(B2A_ERR_INVALID, "empty page table");
+  const int64_t blocks = std::min<int64_t>((n + 255) / 256, 4096);
+  b2a::page_table_scatter_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      page_table, table_stride, table_rows, rows, cols, values, n);
+  return check_launch("page_table_scatter_kernel");
 }
 
 int b2a_decode_num_ctas(int Hq, int Hkv, int D, int dtype, int* num_ctas) {

@@ -60,6 +60,11 @@ SIGNATURES = {
         [_P, _P, c_int, c_int, c_int, _P, _P, c_int, _P, ctypes.POINTER(c_int),
          ctypes.POINTER(c_int)],
     ),
+    "b2a_decode_metadata": (
+        c_int,
+        [_P, c_int64, c_int64, _P, _P, c_int, c_int, c_int, _P, _P, c_int64, _P, _P, _P, c_int, _P, _P, _P],
+    ),
+    "b2a_page_table_scatter": (c_int, [_P, c_int64, c_int64, _P, _P, _P, c_int64, _P]),
     "b2a_decode_num_ctas": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_int)]),
     "b2a_decode_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
     "b2a_decode": (

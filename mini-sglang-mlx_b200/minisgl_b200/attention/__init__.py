@@ -7,7 +7,7 @@ ValueError with the same message shape.
 
 from __future__ import annotations
 
-from .b200 import B200AttnBackend, B200DecodeMetadata, B200PrefillMetadata, paged_decode_attention
+from .b200 import B200AttnBackend, B200DecodeMetadata, B200PrefillMetadata, page_table_scatter, paged_decode_attention
 from .base import BaseAttnBackend, PinnedStager, paged_kv_indices
 
 SUPPORTED_ATTENTION_BACKENDS = {
@@ -30,5 +30,6 @@ __all__ = [
     "SUPPORTED_ATTENTION_BACKENDS",
     "create_attention_backend",
     "paged_decode_attention",
+    "page_table_scatter",
     "paged_kv_indices",
 ]

@@ -41,6 +41,7 @@ class B200DecodeMetadata:
     page_size: int
     batch_size: int
     workspace: torch.Tensor | None = None  # fixed split-partial workspace (CUDA-graph metadata)
+    counts: torch.Tensor | None = None  # int32 [2] segments, split partials (device-built metadata)
 
 
 @dataclass
@@ -164,6 +165,7 @@ class B200AttnBackend(BaseAttnBackend):
             kv_last_page_len=torch.zeros(batch_size, **i32), cta_indptr=torch.zeros(nc + 1, **i32),
             segs=torch.zeros((cap + 1, 4), **i32), merge_indptr=torch.zeros(batch_size + 1, **i32),
             n_partials=cap, num_ctas=nc, page_size=self.page_size, batch_size=batch_size, workspace=ws,
+            counts=torch.zeros(2, **i32),
         )
 
     def fill_decode_graph_metadata(self, meta: B200DecodeMetadata, rows: np.ndarray, lens: np.ndarray) -> None:
@@ -179,6 +181,27 @@ class B200AttnBackend(BaseAttnBackend):
             [kv_indptr, kv_indices, lpl, cta_indptr, segs, merge_indptr], self.device,
             out=[meta.kv_indptr, meta.kv_indices[: kv_indices.size], meta.kv_last_page_len, meta.cta_indptr,
                  meta.segs[: segs.shape[0]], meta.merge_indptr])
+
+    def build_decode_metadata_device(self, meta: B200DecodeMetadata, page_table: torch.Tensor,
+                                     rows: torch.Tensor, lens: torch.Tensor) -> None:
+        """Fill ``meta`` (from ``alloc_decode_graph_metadata``) on the device (b2a_decode_metadata).
+
+        ``page_table`` is a device int32 copy of the engine's page table, ``rows``
+        and ``lens`` device int32 ``[meta.batch_size]``. Replaces the host CSR of
+        attention/metal.py:145-152 and the host split plan; stream-ordered and
+        capturable in a CUDA graph. The values equal ``fill_decode_graph_metadata``'s
+        for the same rows and lengths.
+        """
+        B = meta.batch_size
+        assert page_table.dtype == torch.int32 and page_table.is_contiguous() and page_table.dim() == 2
+        assert rows.dtype == torch.int32 and lens.dtype == torch.int32 and rows.numel() >= B and lens.numel() >= B
+        nat.call(
+            "b2a_decode_metadata", page_table.data_ptr(), page_table.shape[0], page_table.shape[1],
+            rows.data_ptr(), lens.data_ptr(), B, meta.page_size, meta.num_ctas,
+            meta.kv_indptr.data_ptr(), meta.kv_indices.data_ptr(), meta.kv_indices.numel(),
+            meta.kv_last_page_len.data_ptr(), meta.cta_indptr.data_ptr(), meta.segs.data_ptr(), meta.segs.shape[0],
+            meta.merge_indptr.data_ptr(), meta.counts.data_ptr(), current_stream_ptr(self.device),
+        )
 
     def forward_decode(self, q: torch.Tensor, layer_id: int, meta: B200DecodeMetadata) -> torch.Tensor:
         B = meta.batch_size
@@ -318,3 +341,18 @@ def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.
         current_stream_ptr(q.device),
     )
     return out
+
+
+def page_table_scatter(page_table: torch.Tensor, rows: torch.Tensor, cols: torch.Tensor, values: torch.Tensor) -> None:
+    """``page_table[rows[i], cols[i]] = values[i]`` on the device (b2a_page_table_scatter).
+
+    Applies the slots a step allocated on the host to a device copy of the page
+    table (the input of ``build_decode_metadata_device``). All int32, same device.
+    """
+    assert page_table.dtype == torch.int32 and page_table.is_contiguous() and page_table.dim() == 2
+    n = rows.numel()
+    assert cols.numel() == n and values.numel() == n
+    for t in (rows, cols, values):
+        assert t.dtype == torch.int32 and t.is_contiguous()
+    nat.call("b2a_page_table_scatter", page_table.data_ptr(), page_table.shape[0], page_table.shape[1],
+             rows.data_ptr(), cols.data_ptr(), values.data_ptr(), n, current_stream_ptr(page_table.device))

@@ -6,11 +6,14 @@ needs for the step. The decode forward (token gather from the device token
 pool, embeddings, all layers with fused RoPE + KV store and split-KV
 attention, final norm, LM head, argmax) is therefore captured once per bucket
 of a batch-size ladder and replayed. Per step the host only writes the
-bucket's static inputs -- page-table rows, positions, KV slots -- and
-rewrites its attention metadata in place (fixed-capacity buffers, see
-``B200AttnBackend.alloc_decode_graph_metadata``); a batch is padded up to
-its bucket with one-token requests on a reserved pad row whose page is a
-reserved pad page of the pool, so padding computes real, discarded values.
+bucket's static inputs -- page-table rows, lengths, positions, KV slots.
+With the engine's device page table the graph itself applies the new slots
+to it and builds the attention metadata from it (b2a_page_table_scatter,
+b2a_decode_metadata); without it the host rewrites the metadata in place
+(fixed-capacity buffers, see ``B200AttnBackend.alloc_decode_graph_metadata``).
+A batch is padded up to its bucket with one-token requests on a reserved pad
+row whose page is a reserved pad page of the pool, so padding computes real,
+discarded values.
 """
 
 from __future__ import annotations
@@ -20,6 +23,7 @@ from typing import Dict, List
 import numpy as np
 import torch
 
+from ..attention import page_table_scatter
 from ..attention.base import PinnedStager
 from ..core import Batch
 
@@ -38,6 +42,8 @@ class DecodeGraphs:
         self.rows = torch.full((bmax,), pad_row, dtype=torch.int32, device=dev)
         self.positions = torch.zeros(bmax, dtype=torch.int32, device=dev)
         self.out_loc = torch.full((bmax,), pad_slot, dtype=torch.int32, device=dev)
+        self.lens = torch.ones(bmax, dtype=torch.int32, device=dev)
+        self.page_table_dev = engine.page_table_dev  # None: metadata built on the host
         self._stager = PinnedStager(slots=4)
         self.graphs: Dict[int, torch.cuda.CUDAGraph] = {}
         self.metas: Dict[int, object] = {}
@@ -63,6 +69,9 @@ class DecodeGraphs:
             rows = self.rows[:b]
 
             def step():
+                if self.page_table_dev is not None:
+                    page_table_scatter(self.page_table_dev, rows, batch.positions, batch.out_loc)
+                    be.build_decode_metadata_device(meta, self.page_table_dev, rows, self.lens[:b])
                 with eng.ctx.forward_batch(batch):
                     logits = eng.model(self.token_pool[rows.long()])
                 return torch.argmax(logits, dim=-1).to(torch.int32)
@@ -87,8 +96,12 @@ class DecodeGraphs:
         lens_p = np.concatenate([lens, np.ones(pad, dtype=np.int64)])
         pos_p = np.concatenate([positions, np.zeros(pad, dtype=np.int32)]).astype(np.int32)
         loc_p = np.concatenate([out_loc, np.full(pad, self.pad_slot)]).astype(np.int32)
-        self._stager.upload([rows_p, pos_p, loc_p], self.engine.device,
-                            out=[self.rows[:b], self.positions[:b], self.out_loc[:b]])
-        self.engine.attn_backend.fill_decode_graph_metadata(self.metas[b], rows_p, lens_p)
+        if self.page_table_dev is not None:
+            self._stager.upload([rows_p, pos_p, loc_p, lens_p.astype(np.int32)], self.engine.device,
+                                out=[self.rows[:b], self.positions[:b], self.out_loc[:b], self.lens[:b]])
+        else:
+            self._stager.upload([rows_p, pos_p, loc_p], self.engine.device,
+                                out=[self.rows[:b], self.positions[:b], self.out_loc[:b]])
+            self.engine.attn_backend.fill_decode_graph_metadata(self.metas[b], rows_p, lens_p)
         self.graphs[b].replay()
         return self.outs[b][:n]

@@ -28,7 +28,7 @@ from typing import Dict, List, Sequence, Tuple
 import numpy as np
 import torch
 
-from ..attention import create_attention_backend
+from ..attention import create_attention_backend, page_table_scatter
 from ..attention.base import PinnedStager
 from ..core import Batch, Context, Req, SamplingParams, batch_positions_out_loc, set_global_ctx
 from ..kvcache import MHAKVCache
@@ -55,6 +55,9 @@ class EngineConfig:
     cache_type: str = "radix"
     overlap_scheduling: bool = True
     cuda_graph_max_bs: int = 128  # decode batches up to this size replay CUDA graphs (0: eager)
+    # keep a device copy of the page table; CUDA-graph decode steps then build their
+    # attention metadata on the device, inside the graph (b2a_decode_metadata)
+    device_metadata: bool = True
     seed: int = 42
 
 
@@ -77,6 +80,8 @@ class Engine:
         self.pad_row = cfg.max_running_req
         self.page_table = np.zeros((cfg.max_running_req + 1, self.max_seq_len), dtype=np.int32)
         self.page_table[self.pad_row, :P] = self.pad_slot + np.arange(P, dtype=np.int32)
+        # device copy, kept current by the scheduler with the slots each step allocates
+        self.page_table_dev = torch.from_numpy(self.page_table).to(self.device) if cfg.device_metadata else None
         self.ctx = Context(page_size=cfg.page_size)
         self.ctx.page_table = self.page_table
         self.ctx.kv_cache = self.kv_cache
@@ -153,7 +158,21 @@ class Scheduler:
         arrays = [positions, out_loc, rows]
         if batch.is_prefill:
             arrays.append(np.concatenate([r.input_ids[r.cached_len: r.device_len] for r in reqs]).astype(np.int32))
+        mirror = self.engine.page_table_dev is not None
+        if mirror:
+            # page-table entries this step makes valid, for the device copy: a decode
+            # token's new slot; a prefill request's whole row so far (its prefix-cache
+            # hit was written on the host when it was admitted)
+            if batch.is_decode:
+                arrays += [rows, positions, out_loc]
+            else:
+                lens = np.array([r.device_len for r in reqs], dtype=np.int64)
+                cols = np.concatenate([np.arange(n, dtype=np.int32) for n in lens.tolist()])
+                r_tok = np.repeat(rows, lens)
+                arrays += [r_tok, cols, self.engine.page_table[r_tok, cols]]
         dev = self._stager.upload(arrays, self.engine.device)
+        if mirror:
+            page_table_scatter(self.engine.page_table_dev, *dev[-3:])
         self.num_steps[batch.phase] += 1
         if batch.is_prefill:
             self.num_prefill_tokens += len(positions)

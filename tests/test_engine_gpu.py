@@ -30,8 +30,11 @@ def _prompts(rng):
     ]
 
 
-@pytest.mark.parametrize("overlap,graphs", [(True, True), (False, True), (True, False)])
-def test_engine_fp32_tokens_match_oracle(overlap, graphs):
+@pytest.mark.parametrize("overlap,graphs,device_meta",
+                         [(True, True, True), (False, True, True), (True, False, True), (True, True, False)])
+def test_engine_fp32_tokens_match_oracle(overlap, graphs, device_meta):
+    """Greedy tokens identical to the fp64 recompute oracle, with and without overlap
+    scheduling, decode CUDA graphs and the device-built decode metadata."""
     import torch
 
     from minisgl_b200.core import SamplingParams
@@ -43,7 +46,7 @@ def test_engine_fp32_tokens_match_oracle(overlap, graphs):
     max_tokens = [int(x) for x in rng.integers(8, 20, len(prompts))]
     cfg = EngineConfig(spec=tiny_spec(num_layers=2, vocab_size=500), dtype="float32", max_running_req=4,
                        page_size=16, num_tokens=8192, max_extend_tokens=256, overlap_scheduling=overlap,
-                       cuda_graph_max_bs=4 if graphs else 0)
+                       cuda_graph_max_bs=4 if graphs else 0, device_metadata=device_meta)
     llm = LLM(cfg)
     outs = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in max_tokens])
     torch.cuda.synchronize()
