@@ -164,9 +164,18 @@ __device__ __forceinline__ bool tc_wait(uint64_t* bar, uint32_t parity, volatile
 // overwritten and O_t may be rescaled by the softmax warps of tile t without
 // waiting on anything else, and S_t(j+1) never overwrites a P_t still in use.
 // The softmax releases P_t(j) in two halves (keys 0-63, then 64-127; one
-// mbarrier each), so the first four PV MMAs of the tile run while it
-// finishes the block: the S -> softmax -> PV -> S chain of a tile is what
-// bounds this kernel, the tensor pipe itself runs at full rate.
+// mbarrier each), so the first four PV MMAs of the tile can run while it
+// finishes the block.
+// The single issuing thread is what bounds this kernel: the tensor pipe keeps
+// no queue of its MMAs, so every instruction between two MMA groups is idle
+// pipe time, and an mbarrier wait costs ~110-240 clk even on a completed phase
+// (in-kernel clock stamps: the issuer spends ~3300 clk per block on 24 MMAs
+// worth 1536 clk, while the softmax warps idle ~1800 clk per block). Each
+// release therefore also bumps a shared-memory count after the arrive; the
+// issuer first reads the second half's count with one acquire load (~40 clk)
+// and, when both halves are written, issues all eight PV MMAs with no wait.
+// Only a P that is not ready yet costs an mbarrier wait (a suspended thread,
+// not a spin that would take issue slots from the softmax warps).
 constexpr int kTc2Threads = 384;
 
 struct Tc2Smem {
@@ -181,7 +190,8 @@ struct Tc2Smem {
   static constexpr int NBARS = 22;
   static constexpr uint32_t TMEM_SLOT = BARS + NBARS * 8;
   static constexpr uint32_t ABORT = TMEM_SLOT + 8;
-  static constexpr uint32_t TOTAL = ABORT + 8;
+  static constexpr uint32_t PCNT = ABORT + 8;  // u32 [8]: P releases counted per (tile, half)
+  static constexpr uint32_t TOTAL = PCNT + 32;
   static constexpr uint32_t ALLOC = TOTAL + 1024;
 };
 
@@ -230,6 +240,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
   uint64_t* mma_done = bars + 13;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + Tc2Smem::TMEM_SLOT);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + Tc2Smem::ABORT);
+  uint32_t* pcnt = reinterpret_cast<uint32_t*>(smem + Tc2Smem::PCNT);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.G;
@@ -266,6 +277,7 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
       for (int c = 0; c < 2; ++c) mbar_init(&p_full[i * 4 + c], 4);  // one arrive per softmax warp
     }
     mbar_init(mma_done, 1);
+    for (int i = 0; i < 8; ++i) pcnt[i] = 0;
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -344,6 +356,13 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
         }
         tc_commit(&s_full[t]);
       };
+      // P(j) of (tile, half) released by all 4 softmax warps: an acquire load of
+      // the release count (~40 clk) instead of an mbarrier wait (~160 clk)
+      auto p_done = [&](int idx, int j) -> bool {
+        uint32_t v;
+        asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_u32(&pcnt[idx])) : "memory");
+        return v >= 4u * (uint32_t)(j + 1);
+      };
       // PV K-steps 4 half .. 4 half + 3 read the P columns of one half
       auto issue_pv = [&](int t, int j, int half) {
         const uint32_t sV = smem_u32(smem + Tc2Smem::V0 + (j & 1) * kTcTileBytes);
@@ -372,13 +391,19 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
         bool k_next = false;
         for (int t = 0; t < 2 && ok; ++t) {
           if (j < nb_t[t]) {
-            for (int half = 0; half < 2 && ok; ++half) {
-              if (!tc_wait(&p_full[t * 4 + half], (uint32_t)j & 1u, abort_flag)) {
-                ok = false;
-                break;
-              }
+            if (p_done(t * 4 + 1, j)) {
               tc_fence_after();
-              issue_pv(t, j, half);
+              issue_pv(t, j, 0);
+              issue_pv(t, j, 1);
+            } else {
+              for (int half = 0; half < 2 && ok; ++half) {
+                if (!p_done(t * 4 + half, j) && !tc_wait(&p_full[t * 4 + half], (uint32_t)j & 1u, abort_flag)) {
+                  ok = false;
+                  break;
+                }
+                tc_fence_after();
+                issue_pv(t, j, half);
+              }
             }
             if (!ok) break;
           }
@@ -506,7 +531,12 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
           tmem_wait_st();
           tc_fence_before();
           __syncwarp();
-          if (lane == 0) mbar_arrive(&p_full[t * 4 + (c >> 1)]);
+          if (lane == 0) {
+            // the arrive first, then the counted release: a reader that sees the
+            // count also sees the barrier phase complete
+            mbar_arrive(&p_full[t * 4 + (c >> 1)]);
+            asm volatile("red.release.cta.shared::cta.add.u32 [%0], 1;" ::"r"(smem_u32(&pcnt[t * 4 + (c >> 1)])) : "memory");
+          }
         }
         if (c < 3) tmem_wait_ld();
       }
