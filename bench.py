@@ -213,6 +213,8 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
     if world > 1:
         dist.barrier()
     evs = []
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    clocks.start()
     for _ in range(max(5, min(steps, 20))):
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record()
@@ -220,6 +222,7 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
         b.record()
         evs.append((a, b))
     torch.cuda.synchronize()
+    clk = clocks.stop()
     ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     nbytes = decode_bytes(pb.lens, P, Hq, Hkv, D, 2)
     stats = torch.tensor([ms], dtype=torch.float64, device=dev)
@@ -236,6 +239,7 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
                      "n_partials": meta.n_partials, "pool_gb": round(need / 1e9, 1)},
            "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(gbs / peak, 4), "peak_kind": kind},
+           "clocks_rank0": clk,
            "config": {"workload": "config5: Qwen3-8B attention (32q/8kv/128), bf16, page 16, 1024 seqs, "
                                   "L log-uniform [1024, 131072], split-KV, request-partitioned",
                       "sum_ctx_tokens_all": int(lens_all.sum())}}
@@ -361,7 +365,11 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
         be._forward_prefill(q, None, None, 0, meta)
     torch.cuda.synchronize()
     evs, revs = [], []
-    for _ in range(steps):
+    # at least 50 calls (~13 ms) so that the clock sampler sees the timed region
+    n_iter = max(steps, 50)
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    clocks.start()
+    for _ in range(n_iter):
         r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         r0.record()
         rope.rope_store_(q, knew, vnew, pos_t, loc_t, kv, 0)
@@ -373,6 +381,7 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
         b.record()
         evs.append((a, b))
     torch.cuda.synchronize()
+    clk = clocks.stop()
     ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
     rope_ms = float(np.mean([a.elapsed_time(b) for a, b in revs]))
     rope_bytes = rope_store_bytes(T, Hq, Hkv, D, 2)
@@ -388,7 +397,8 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
 
     tile = nat.extend_tile_q(Hq, Hkv, D, nat.B2A_DTYPE_BF16, pb.page_size)
     return {"metric": "extend attention TFLOP/s (causal, visible keys only)", "value": round(tf, 2),
-            "unit": "TFLOP/s", "ms_per_call": round(ms, 4), "flops_per_call": flops,
+            "unit": "TFLOP/s", "ms_per_call": round(ms, 4), "flops_per_call": flops, "calls_timed": n_iter,
+            "clocks": clk,
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tf / peak, 4), "peak_kind": kind + " (bf16 dense, burst)"},
             "config": {"workload": "config3: 32 ragged requests, prefix U[0,4096] page-aligned (+1 unaligned), "
@@ -632,8 +642,8 @@ def run_ours(args):
     set_global_ctx(None)
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
-    c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps)
     ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
+    c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps)
     e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed)
 
     line = None
