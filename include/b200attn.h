@@ -263,6 +263,18 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
                int T, int B, int Hq, int Hkv, int D, float scale, void* out, int dtype,
                void* stream);
 
+/* ------------------------------------------------------------------------
+ * SwiGLU activation of the engine harness's MLP.
+ * Replaces `swiglu(gate, up)` (python/minisgl_mlx/models/transformer.py:26-30,
+ * fused by mx.compile) called from MLP.__call__ (:67-69). Row r of gate_up
+ * holds [gate (F) | up (F)] starting at gate_up + r * row_stride elements;
+ *   out[r * F + i] = silu(gate[i]) * up[i]
+ * in fp32 with silu(gate) rounded to the storage type before the product, as
+ * the unfused `silu(gate) * up` does. F must be even; dtype f32, bf16 or f16.
+ * ------------------------------------------------------------------------ */
+int b2a_swiglu(const void* gate_up, int64_t row_stride, void* out, int64_t rows, int F, int dtype,
+               void* stream);
+
 #ifdef __cplusplus
 }
 #endif

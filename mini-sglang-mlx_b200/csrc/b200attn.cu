@@ -18,6 +18,7 @@
 #include "pack_kv.cuh"
 #include "metadata.cuh"
 #include "rope_store.cuh"
+#include "swiglu.cuh"
 
 namespace {
 
@@ -624,6 +625,23 @@ int b2a_pack_kv(const void* k_pool, const void* v_pool, int64_t num_slots, const
   if (blocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many rows");
   b2a::pack_kv_kernel<<<(unsigned)blocks, 256, 0, reinterpret_cast<cudaStream_t>(stream)>>>(a);
   return check_launch("pack_kv_kernel");
+}
+
+int b2a_swiglu(const void* gate_up, int64_t row_stride, void* out, int64_t rows, int F, int dtype, void* stream) {
+  if (rows < 0 || F < 0) return fail(B2A_ERR_INVALID, "negative size");
+  if (rows == 0 || F == 0) return ok();
+  if (F % 2) return fail(B2A_ERR_INVALID, "F = %d must be even", F);
+  if (row_stride < 2 * (int64_t)F) return fail(B2A_ERR_INVALID, "row_stride %lld < 2F", (long long)row_stride);
+  if (!gate_up || !out) return fail(B2A_ERR_INVALID, "NULL pointer argument");
+  const int64_t n = rows * (F / 2);
+  const unsigned blocks = (unsigned)std::min<int64_t>((n + 255) / 256, 148 * 16);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  return with_dtype<true>(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    b2a::swiglu_kernel<T><<<blocks, 256, 0, st>>>(reinterpret_cast<const T*>(gate_up), row_stride,
+                                                   reinterpret_cast<T*>(out), rows, F);
+    return check_launch("swiglu_kernel");
+  });
 }
 
 int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,

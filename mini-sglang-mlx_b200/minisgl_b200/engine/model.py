@@ -9,7 +9,10 @@ RMSNorm and tied embeddings as the LM head. Prefill keeps only each
 request's last token before the head (``attn_metadata.last_indices``).
 
 Inputs are packed ``[T]`` token ids. GEMMs are cuBLAS through ``F.linear``;
-weights are drawn N(0, 0.02) from a seeded generator (there are no
+the two residual adds of a layer are folded into the o_proj and down GEMMs
+(``torch.addmm`` with beta = 1: one rounding instead of two), and SwiGLU is
+one library kernel (``b2a_swiglu``), as the reference's mx.compile'd
+``swiglu`` is one kernel. Weights are drawn N(0, 0.02) from a seeded generator (there are no
 checkpoints on this machine), norms start at 1.
 """
 
@@ -21,9 +24,23 @@ from typing import List
 import torch
 import torch.nn.functional as F
 
+from .. import _native as nat
 from ..config import ModelConfig, RotaryConfig
 from ..core import get_global_ctx
+from ..kvcache.pool import dtype_code
 from ..layers import AttentionLayer
+
+
+def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up of a ``[T, 2F]`` gate/up projection in one kernel (b2a_swiglu).
+
+    Reference: python/minisgl_mlx/models/transformer.py:26-30 and :67-69.
+    """
+    T, F2 = gate_up.shape
+    out = torch.empty((T, F2 // 2), dtype=gate_up.dtype, device=gate_up.device)
+    nat.call("b2a_swiglu", gate_up.data_ptr(), gate_up.stride(0), out.data_ptr(), T, F2 // 2,
+             dtype_code(gate_up.dtype), torch.cuda.current_stream().cuda_stream)
+    return out
 
 
 @dataclass(frozen=True)
@@ -99,10 +116,9 @@ class Qwen3Model:
             k = qkv[:, Hq * D: (Hq + Hkv) * D].view(T, Hkv, D)
             v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
             # q/k RMSNorm fused into the RoPE + KV-store kernel
-            h = h + F.linear(L.attn(q, k, v, L.q_norm, L.k_norm, eps), L.o)
+            h = torch.addmm(h, L.attn(q, k, v, L.q_norm, L.k_norm, eps), L.o.t())
             x = F.rms_norm(h, (spec.hidden_size,), L.post_norm, eps)
-            gate, up = F.linear(x, L.gate_up).chunk(2, dim=-1)
-            h = h + F.linear(F.silu(gate) * up, L.down)
+            h = torch.addmm(h, swiglu(F.linear(x, L.gate_up)), L.down.t())
         if batch.is_prefill:
             h = h[batch.attn_metadata.last_indices.long()]
         h = F.rms_norm(h, (spec.hidden_size,), self.norm, eps)
