@@ -331,6 +331,26 @@ def extend_flops(prefix: np.ndarray, extend: np.ndarray, Hq: int, D: int) -> flo
     return 4.0 * Hq * D * vis
 
 
+def extend_executed_flops(prefix: np.ndarray, extend: np.ndarray, Hq: int, Hkv: int, D: int) -> float:
+    """FLOPs the tcgen05 extend kernel executes: whole 128-row tiles x whole 128-key blocks.
+
+    A work item is two tiles of 128/G query tokens (G query heads each) of one request;
+    tile t runs over every 128-key block up to the last key visible to its last row.
+    """
+    G = Hq // Hkv
+    TT, KB = 128 // G, 128
+    blocks = 0
+    for p, e in zip(prefix, extend):
+        p, e = int(p), int(e)
+        for tb in range(0, e, 2 * TT):
+            nq = min(e - tb, 2 * TT)
+            for t, nqt in enumerate((min(nq, TT), max(0, nq - TT))):
+                if nqt:
+                    blocks += (min(p + e, p + tb + t * TT + nqt) + KB - 1) // KB
+    # per block: S = Q K^T and O += P V, each 2 x 128 x 128 x D flops, for every kv head
+    return float(blocks) * Hkv * 2 * (2 * 128 * KB * D)
+
+
 def measure_extend(dev, seed: int, steps: int, warmup: int):
     """Config 3: 32 ragged requests with a cached radix prefix, fused RoPE+store then extend attention."""
     import torch
@@ -396,8 +416,14 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
     from minisgl_b200 import _native as nat
 
     tile = nat.extend_tile_q(Hq, Hkv, D, nat.B2A_DTYPE_BF16, pb.page_size)
+    tc = tile == 2 * (128 // (Hq // Hkv))
+    # tile-padded work the tensor cores run (partial query tiles, masked key blocks)
+    exe = extend_executed_flops(eb.prefix, eb.extend, Hq, Hkv, D) if tc else None
     return {"metric": "extend attention TFLOP/s (causal, visible keys only)", "value": round(tf, 2),
             "unit": "TFLOP/s", "ms_per_call": round(ms, 4), "flops_per_call": flops, "calls_timed": n_iter,
+            "executed": None if exe is None else {
+                "flops_per_call": exe, "tflops": round(exe / (ms * 1e-3) / 1e12, 2),
+                "frac_of_peak": round(exe / (ms * 1e-3) / 1e12 / peak, 4), "useful_share": round(flops / exe, 4)},
             "clocks": clk,
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tf / peak, 4), "peak_kind": kind + " (bf16 dense, burst)"},

@@ -269,6 +269,25 @@ int b2a_qknorm_rope_store(void* q, int64_t q_row_stride, void* q_out, void* k, i
   a.Hkv = Hkv;
   a.D = D;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  // token-major fast path: 16-bit rows, D = rot_dim = 128, every row and pointer on
+  // 16 bytes (bit-identical rotation; see rope_store_tok_kernel)
+  const bool tok_path = (dtype == B2A_DTYPE_BF16 || dtype == B2A_DTYPE_F16) && D == 128 && rot_dim == 128 &&
+                        aligned(k, 16) && k_row_stride % 8 == 0 && (a.Hq == 0 || (aligned(q, 16) && q_row_stride % 8 == 0)) &&
+                        (!q_out || aligned(q_out, 16)) && aligned(inv_freq, 16) &&
+                        (!q_norm_w || aligned(q_norm_w, 16)) && (!k_norm_w || aligned(k_norm_w, 16)) &&
+                        (!store || (aligned(v, 16) && v_row_stride % 8 == 0 && aligned(k_pool, 16) && aligned(v_pool, 16)));
+  if (tok_path) {
+    const int ng = (a.Hq + Hkv + 3) / 4;
+    // warps per token: enough warps for 148 SMs at small T, one per token at large T
+    const int W = (int)std::max<int64_t>(1, std::min<int64_t>({8, (int64_t)ng, (2368 + T - 1) / T}));
+    const int64_t tblocks = ((int64_t)T * W + 7) / 8;
+    if (tblocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many tokens");
+    if (dtype == B2A_DTYPE_BF16)
+      b2a::rope_store_tok_kernel<__nv_bfloat16><<<(unsigned)tblocks, 256, 0, st>>>(a, W);
+    else
+      b2a::rope_store_tok_kernel<__half><<<(unsigned)tblocks, 256, 0, st>>>(a, W);
+    return check_launch("rope_store_tok_kernel");
+  }
   const int64_t rows = (int64_t)T * (a.Hq + 2 * Hkv);
   const int64_t blocks = (rows + 7) / 8;
   if (blocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many rows");

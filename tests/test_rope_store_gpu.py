@@ -174,3 +174,48 @@ def test_qknorm_rope_store(dtype, q_out):
     # the pool holds exactly the returned k and the untouched v
     assert np.array_equal(to_np(kv.k[0])[out_loc], to_np(k))
     assert np.array_equal(to_np(kv.v[0])[out_loc], hv)
+
+
+@pytest.mark.parametrize("dtype", ["bfloat16", "float16"])
+@pytest.mark.parametrize("T,Hq,Hkv", [(3000, 16, 8), (37, 32, 8), (5, 4, 1)])
+@pytest.mark.parametrize("norm", [False, True])
+def test_token_path_matches_row_path(dtype, T, Hq, Hkv, norm):
+    """The token-major fast path (16-bit, D = rot = 128, rows on 16 bytes) against the
+    row-per-warp kernel, which a row stride that is not a multiple of 8 elements selects.
+    Covers one warp per token (large T), several warps per token, and more q/k rows than
+    one register pass holds (32q/8kv)."""
+    import torch
+
+    from minisgl_b200.config import RotaryConfig
+    from minisgl_b200.kvcache import MHAKVCache
+    from minisgl_b200.layers import RotaryEmbedding
+
+    D, N, eps = 128, 4096, 1e-6
+    rng, qkv, positions, out_loc = _setup(T, Hq, Hkv, D, dtype, max(N, T), seed=11)
+    N = max(N, T)
+    W = (Hq + 2 * Hkv) * D
+    rope = RotaryEmbedding(RotaryConfig(D, D, 1e6, 131072))
+    wq = to_dev(O.round_to(rng.uniform(0.5, 1.5, D).astype(np.float32), dtype), dtype) if norm else None
+    wk = to_dev(O.round_to(rng.uniform(0.5, 1.5, D).astype(np.float32), dtype), dtype) if norm else None
+    pos_d, loc_d = torch.from_numpy(positions).cuda(), torch.from_numpy(out_loc).cuda()
+    outs = []
+    for pad in (0, 1):  # pad 0: fast path; pad 1: odd row stride -> row kernel
+        buf = torch.zeros((T, W + pad), dtype=torch_dtype(dtype), device="cuda")
+        buf[:, :W] = to_dev(qkv, dtype)
+        q = buf[:, : Hq * D].view(T, Hq, D) if pad == 0 else buf[:, : Hq * D].unflatten(1, (Hq, D))
+        k = buf[:, Hq * D:(Hq + Hkv) * D].unflatten(1, (Hkv, D))
+        v = buf[:, (Hq + Hkv) * D: W].unflatten(1, (Hkv, D))
+        kv = MHAKVCache(1, N, Hkv, D, torch_dtype(dtype))
+        rope.rope_store_(q, k, v, pos_d, loc_d, kv, 0, wq, wk, eps)
+        torch.cuda.synchronize()
+        outs.append((q.float().cpu(), k.float().cpu(), kv.k[0].float().cpu(), kv.v[0].float().cpu()))
+    for a, b in zip(outs[0], outs[1]):
+        if norm:
+            # the RMSNorm's sum of squares is added in another order: a normalised element
+            # may move by one ulp, which the rotation carries into outputs of the row's scale
+            # (|x| <~ 4 here); almost every element stays bit-equal
+            ulp = 2.0 ** -7 if dtype == "bfloat16" else 2.0 ** -10
+            assert float((a - b).abs().max()) <= 2 * ulp * 4
+            assert float((a == b).float().mean()) > 0.95
+        else:
+            assert torch.equal(a, b)
