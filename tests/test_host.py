@@ -172,3 +172,15 @@ def test_workload_generators_are_seeded_and_valid():
     assert eb.prefix[0] % 16 != 0 or eb.prefix[0] == 0
     assert all(p % 16 == 0 for p in eb.prefix[1:])
     assert (eb.extend >= 64).all() and (eb.extend <= 512).all()
+
+
+def test_swiglu_rejects_bad_sizes_before_any_launch():
+    # argument checks return before any CUDA call, so they run without a GPU
+    dummy = 16  # never dereferenced: every call below fails or returns before a launch
+    with pytest.raises(ValueError, match="even"):
+        nat.call("b2a_swiglu", dummy, 8, dummy, 4, 3, nat.B2A_DTYPE_BF16, None)
+    with pytest.raises(ValueError, match="row_stride"):
+        nat.call("b2a_swiglu", dummy, 6, dummy, 4, 4, nat.B2A_DTYPE_BF16, None)
+    with pytest.raises(ValueError, match="negative"):
+        nat.call("b2a_swiglu", dummy, 8, dummy, -1, 4, nat.B2A_DTYPE_BF16, None)
+    nat.call("b2a_swiglu", dummy, 8, dummy, 0, 4, nat.B2A_DTYPE_BF16, None)  # nothing to do
