@@ -67,6 +67,26 @@ def test_radix_lock_and_lru_eviction():
     rc.check_integrity()
 
 
+def test_radix_duplicate_insert_keeps_cached_slots_and_split_keeps_refs():
+    rc = RadixPrefixCache(1)
+    _, h = rc.insert_prefix(ids(1, 2, 3, 4), ids(10, 11, 12, 13))
+    # a second request computed the same 4 tokens plus 2 more: its first 4 slots are
+    # redundant (the caller frees them) and the tree keeps the slots it already had
+    dup, h2 = rc.insert_prefix(ids(1, 2, 3, 4, 5, 6), ids(30, 31, 32, 33, 34, 35))
+    assert dup == 4 and h2.cached_len == 6
+    assert h2.get_matched_indices().tolist() == [10, 11, 12, 13, 34, 35]
+    assert rc.size_info == (6, 0)
+    # a lock taken before a split still covers both halves of the split node
+    rc.lock_handle(h)
+    assert rc.size_info == (2, 4)
+    assert rc.match_prefix(ids(1, 2, 9)).handle.cached_len == 2  # splits [1,2,3,4] at 2
+    rc.check_integrity()
+    assert rc.size_info == (2, 4)
+    rc.lock_handle(h, unlock=True)
+    assert rc.size_info == (6, 0)
+    rc.check_integrity()
+
+
 def test_radix_evict_prefers_older_and_frees_parents():
     rc = RadixPrefixCache(1)
     rc.insert_prefix(ids(1, 2, 3, 4), ids(1, 2, 3, 4))
