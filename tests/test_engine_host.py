@@ -12,7 +12,7 @@ from __future__ import annotations
 import numpy as np
 import pytest
 
-from minisgl_b200.core import Batch, SamplingParams
+from minisgl_b200.core import Batch, Req, SamplingParams
 from minisgl_b200.engine.managers import CacheManager, ChunkedReq, DecodeManager, PrefillManager, TableManager
 from minisgl_b200.engine.radix import NaivePrefixCache, RadixPrefixCache
 
@@ -228,3 +228,63 @@ def test_router_splits_an_oversized_group():
     load = np.array([costs[ids].sum() for ids in ranks])
     assert load.min() > 0 and load.max() <= 1.1 * load.mean()  # one giant group is still balanced
     assert route_requests(prompts, costs, 1, 16)[0].tolist() == list(range(64))
+
+
+def _prompt(cm: CacheManager, tokens, row: int) -> Req:
+    """Admit a prompt the way the prefill manager does: match, lock, borrow the slots."""
+    toks = np.array(tokens, dtype=np.int32)
+    h = cm.match_req(toks)
+    cm.lock(h)
+    cm.page_table[row, : h.cached_len] = h.get_matched_indices()
+    return Req(input_ids=toks, table_idx=row, cached_len=h.cached_len, output_len=4, cache_handle=h)
+
+
+def _prefill_and_finish(cm: CacheManager, tokens, row: int = 0) -> Req:
+    r = _prompt(cm, tokens, row)
+    cm.allocate_paged([r])
+    r.complete_one()
+    cm.cache_req(r, finished=True)
+    return r
+
+
+def test_cache_manager_reuse_recomputes_the_last_prompt_token():
+    pt = np.zeros((4, 64), dtype=np.int32)
+    cm = CacheManager(32, 1, pt, "radix")
+    _prefill_and_finish(cm, [1, 2, 3, 4, 5])
+    assert cm.prefix_cache.size_info.evictable_size == 5
+    cm.check_integrity()
+    # the same prompt again: its last token is computed anyway (its logits pick the
+    # next token), so only 4 of the 5 cached tokens are reused
+    same = _prompt(cm, [1, 2, 3, 4, 5], row=2)
+    assert same.cached_len == 4
+    cm.unlock(same.cache_handle)
+    # a longer prompt that starts with the whole cached one reuses all 5
+    longer = _prompt(cm, [1, 2, 3, 4, 5, 6, 7], row=1)
+    assert longer.cached_len == 5
+    cm.allocate_paged([longer])
+    longer.complete_one()
+    cm.cache_req(longer, finished=True)
+    cm.check_integrity()
+    assert cm.prefix_cache.size_info == (7, 0)
+
+
+def test_cache_manager_evicts_cached_prefixes_when_full():
+    pt = np.zeros((4, 64), dtype=np.int32)
+    cm = CacheManager(8, 1, pt, "radix")
+    _prefill_and_finish(cm, [1, 2, 3, 4, 5, 6])
+    assert len(cm.free_slots) == 2 and cm.available_size == 8
+    _prefill_and_finish(cm, [9, 9, 9, 9, 9], row=1)  # needs 5 slots: evicts the old prefix
+    cm.check_integrity()
+    assert cm.prefix_cache.size_info.total_size == 5
+
+
+def test_cache_manager_pages_of_four():
+    pt = np.zeros((4, 64), dtype=np.int32)
+    cm = CacheManager(8, 4, pt, "radix")
+    r = _prefill_and_finish(cm, list(range(10)))  # 10 tokens take 3 pages
+    pages = pt[r.table_idx, :12].reshape(3, 4)
+    assert np.all(pages[:, 0] % 4 == 0) and np.all(pages - pages[:, :1] == np.arange(4))
+    # the 2 full pages go to the prefix cache, the partial third page back to the free list
+    assert cm.prefix_cache.size_info.evictable_size == 8 and len(cm.free_slots) == 6
+    assert np.all(cm.free_slots % 4 == 0)
+    cm.check_integrity()
