@@ -269,7 +269,8 @@ class LLM(Scheduler):
         self._outputs: Dict[int, List[int]] = {}
 
     def on_token(self, req: Req, token: int, finished: bool) -> None:
-        if not (finished and token in self.eos_token_ids):
+        # a request that stopped at EOS does not output the EOS token itself
+        if not (finished and not req.sampling_params.ignore_eos and token in self.eos_token_ids):
             self._outputs[req.uid].append(token)
 
     def _feed(self) -> None:

@@ -85,3 +85,53 @@ def test_engine_bf16_config4_shape_runs_clean():
     nat.call("b2a_device_error", torch.cuda.current_stream().cuda_stream, ctypes.byref(code))
     assert code.value == 0
     llm.engine.shutdown()
+
+
+def _tiny_llm(overlap=True):
+    from minisgl_b200.engine import LLM, EngineConfig, tiny_spec
+
+    cfg = EngineConfig(spec=tiny_spec(num_layers=2, vocab_size=500), dtype="float32", max_running_req=4,
+                       page_size=16, num_tokens=8192, max_extend_tokens=256, overlap_scheduling=overlap,
+                       cuda_graph_max_bs=4)
+    return LLM(cfg)
+
+
+@pytest.mark.parametrize("overlap", [True, False])
+def test_engine_exact_max_tokens(overlap):
+    """1, 2, 3 and 7 new tokens exactly, with and without overlap scheduling (where a
+    request finishing one step earlier has already been put into the next batch)."""
+    from minisgl_b200.core import SamplingParams
+
+    rng = np.random.default_rng(9)
+    lens = [1, 2, 3, 7]
+    prompts = [rng.integers(0, 500, 20).astype(np.int32) for _ in lens]
+    llm = _tiny_llm(overlap)
+    outs = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in lens])
+    assert [len(o["token_ids"]) for o in outs] == lens
+    llm.cache.check_integrity()
+    assert llm.table.available_size == 4
+    llm.engine.shutdown()
+
+
+def test_engine_stops_at_eos_and_returns_resources():
+    """A request stops at the first EOS token, which is not in its output; requests
+    with ignore_eos run to max_tokens; every page and table row is returned."""
+    from minisgl_b200.core import SamplingParams
+
+    rng = np.random.default_rng(5)
+    prompts = [rng.integers(0, 500, int(n)).astype(np.int32) for n in (40, 17, 64)]
+    llm = _tiny_llm()
+    free_run = [o["token_ids"] for o in llm.generate(prompts, [SamplingParams(max_tokens=12, ignore_eos=True)] * 3)]
+    llm.engine.shutdown()
+    eos = free_run[0][4]  # request 0 meets it at its fifth token (or earlier)
+    llm = _tiny_llm()
+    llm.eos_token_ids = {eos}
+    sps = [SamplingParams(max_tokens=12), SamplingParams(max_tokens=12), SamplingParams(max_tokens=12, ignore_eos=True)]
+    outs = [o["token_ids"] for o in llm.generate(prompts, sps)]
+    for i in range(2):
+        want = free_run[i][: free_run[i].index(eos)] if eos in free_run[i] else free_run[i]
+        assert outs[i] == want
+    assert outs[2] == free_run[2]
+    llm.cache.check_integrity()
+    assert llm.table.available_size == 4
+    llm.engine.shutdown()
