@@ -8,6 +8,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "b200attn.h"
@@ -159,6 +160,26 @@ int decode_config(int Hq, int Hkv, int D, size_t es, DecodeCfg& c) {
   return fail(B2A_ERR_UNSUPPORTED, "decode config (Hq %d, Hkv %d, D %d) does not fit in shared memory", Hq, Hkv, D);
 }
 
+// Launch with programmatic stream serialization: the kernel may become resident
+// while the previous kernel of the stream finishes (it waits in
+// pdl_wait_then_release before touching memory), which hides the launch gap
+// between the back-to-back kernels of a layer inside CUDA graphs.
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // Raises a kernel's dynamic shared-memory limit once per (kernel, device), so
 // steady-state launches (and launches inside CUDA graph capture) make no
 // attribute calls.
@@ -180,7 +201,7 @@ template <typename T, int D, int G, int NCW>
 int decode_launch(const b2a::DecodeArgs& a, const DecodeCfg& c, int grid, cudaStream_t st) {
   auto kern = b2a::decode_kernel<T, D, G, NCW>;
   if (int rc = ensure_smem((const void*)kern, c.smem, "decode")) return rc;
-  kern<<<grid, (c.NCW + 1) * 32, c.smem, st>>>(a);
+  launch_pdl(kern, dim3(grid), dim3((c.NCW + 1) * 32), c.smem, st, a);
   return check_launch("decode_kernel");
 }
 
@@ -283,9 +304,9 @@ int b2a_qknorm_rope_store(void* q, int64_t q_row_stride, void* q_out, void* k, i
     const int64_t tblocks = ((int64_t)T * W + 7) / 8;
     if (tblocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many tokens");
     if (dtype == B2A_DTYPE_BF16)
-      b2a::rope_store_tok_kernel<__nv_bfloat16><<<(unsigned)tblocks, 256, 0, st>>>(a, W);
+      launch_pdl(b2a::rope_store_tok_kernel<__nv_bfloat16>, dim3((unsigned)tblocks), dim3(256), 0, st, a, W);
     else
-      b2a::rope_store_tok_kernel<__half><<<(unsigned)tblocks, 256, 0, st>>>(a, W);
+      launch_pdl(b2a::rope_store_tok_kernel<__half>, dim3((unsigned)tblocks), dim3(256), 0, st, a, W);
     return check_launch("rope_store_tok_kernel");
   }
   const int64_t rows = (int64_t)T * (a.Hq + 2 * Hkv);
@@ -293,7 +314,7 @@ int b2a_qknorm_rope_store(void* q, int64_t q_row_stride, void* q_out, void* k, i
   if (blocks > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many rows");
   return with_dtype<true>(dtype, [&](auto tag) {
     using Tt = decltype(tag);
-    b2a::rope_store_kernel<Tt><<<(unsigned)blocks, 256, 0, st>>>(a);
+    launch_pdl(b2a::rope_store_kernel<Tt>, dim3((unsigned)blocks), dim3(256), 0, st, a);
     return check_launch("rope_store_kernel");
   });
 }
@@ -504,7 +525,8 @@ static int decode_common(const void* q, const void* k_pool, const void* v_pool, 
         if (r) return r;
         if (n_partials > 0) {
           const int blocks = (B * Hq + 3) / 4;
-          b2a::decode_merge_kernel<Tt, Dc><<<blocks, 128, 0, st>>>(a.ws_acc, a.ws_ml, merge_indptr, out, B, Hq);
+          launch_pdl(b2a::decode_merge_kernel<Tt, Dc>, dim3(blocks), dim3(128), 0, st, (const float*)a.ws_acc,
+                     (const float*)a.ws_ml, merge_indptr, out, B, Hq);
           return check_launch("decode_merge_kernel");
         }
         return ok();

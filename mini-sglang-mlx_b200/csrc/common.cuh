@@ -32,6 +32,16 @@ enum WatchdogCode : int {
 
 __device__ __forceinline__ void watchdog_set(int code) { atomicCAS(&g_watchdog, 0, code); }
 
+// Programmatic dependent launch: kernels launched with the programmatic-stream-
+// serialization attribute may become resident while the previous kernel of the
+// stream still runs. This waits (first, before touching any memory) until that
+// kernel has completed and its writes are visible, then lets the next kernel of the
+// stream become resident in turn. Without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_wait_then_release() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- dtypes
 template <typename T>
 struct DT;

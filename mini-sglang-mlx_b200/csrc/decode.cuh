@@ -239,6 +239,7 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* 
 
 template <typename T, int D, int G, int NCW>
 __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeArgs a) {
+  pdl_wait_then_release();
   constexpr int EPT = D / 32;
   constexpr int TG = decode_tg<G>();
   constexpr int REM = 5 - ilog2c(TG * G);
@@ -499,6 +500,7 @@ __global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restri
                                                            const float* __restrict__ ws_ml,
                                                            const int32_t* __restrict__ merge_indptr, void* out,
                                                            int B, int Hq) {
+  pdl_wait_then_release();
   constexpr int EPT = D / 32;
   const int lane = threadIdx.x & 31;
   const int idx = blockIdx.x * 4 + (threadIdx.x >> 5);

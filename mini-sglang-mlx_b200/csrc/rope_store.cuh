@@ -45,6 +45,7 @@ struct RopeStoreArgs {
 
 template <typename T>
 __global__ void __launch_bounds__(256) rope_store_kernel(RopeStoreArgs a) {
+  pdl_wait_then_release();
   const int lane = threadIdx.x & 31;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int rows_per_tok = a.Hq + 2 * a.Hkv;
@@ -163,6 +164,7 @@ __device__ __forceinline__ uint4 pack8(const T (&h)[8]) {
 
 template <typename T>
 __global__ void __launch_bounds__(256, 2) rope_store_tok_kernel(RopeStoreArgs a, int W) {
+  pdl_wait_then_release();
   static_assert(sizeof(T) == 2, "16-bit rows only");
   constexpr int D = 128, HALF = 64;
   const int lane = threadIdx.x & 31;
