@@ -184,3 +184,30 @@ def test_swiglu_rejects_bad_sizes_before_any_launch():
     with pytest.raises(ValueError, match="negative"):
         nat.call("b2a_swiglu", dummy, 8, dummy, -1, 4, nat.B2A_DTYPE_BF16, None)
     nat.call("b2a_swiglu", dummy, 8, dummy, 0, 4, nat.B2A_DTYPE_BF16, None)  # nothing to do
+
+
+def test_extend_executed_flops_counts_whole_tiles_and_blocks():
+    """bench.extend_executed_flops against a brute-force walk of the tcgen05 kernel's
+    work: items of two 128/G-token tiles, each over whole 128-key blocks up to the last
+    key its last row sees; never less than the visible-key FLOPs."""
+    import bench
+
+    rng = np.random.default_rng(2)
+    Hq, Hkv, D = 16, 8, 128
+    G = Hq // Hkv
+    prefix = rng.integers(0, 700, 9) // 16 * 16
+    extend = rng.integers(1, 400, 9)
+    blocks = 0
+    for p, e in zip(prefix, extend):
+        for tok0 in range(0, int(e), 2 * (128 // G)):
+            for t in range(2):
+                first = tok0 + t * (128 // G)
+                last = min(int(e), first + 128 // G) - 1
+                if last < first:
+                    continue
+                keys = int(p) + last + 1  # keys visible to the tile's last row
+                blocks += -(-keys // 128)
+    want = blocks * Hkv * 2 * (2 * 128 * 128 * D)
+    got = bench.extend_executed_flops(prefix, extend, Hq, Hkv, D)
+    assert got == want
+    assert got >= bench.extend_flops(prefix, extend, Hq, D)
