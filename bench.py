@@ -15,7 +15,9 @@ over the cached context (AttentionLayer.__call__, reference layers.py:103-111).
            of every layer's q/k/v from pinned memory, the 28 AttentionLayer
            calls and a D2H read of every layer's output (copies of other layers
            overlap each layer's attention)
-  roofline: decode call (decode kernel + split merge) per launch, CUDA events
+  roofline: one decode call (one decode_kernel launch, split requests merged
+           inside it) per launch, CUDA events; traffic from the committed ncu
+           summary when it was captured on the same decode sources
   cpu_baseline: the CPU oracle port (torch, naive gather + masked SDPA) on one
            layer of the same batch (rank 0, N = 1 only)
   extend_config3 / decode_config5 / e2e_offline_config4: the other configurations
@@ -150,7 +152,7 @@ def cpu_sample(lens, page_table, P, Hq, Hkv, D, num_slots, steps, warmup, seed):
 
     from oracle.cpu_naive import naive_decode_torch
 
-    torch.set_num_threads(os.cpu_count() or 1)
+    torch.set_num_threads(len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1))
     g = torch.Generator().manual_seed(seed)
     k_pool = torch.randn((num_slots, Hkv, D), generator=g).to(torch.bfloat16)
     v_pool = torch.randn((num_slots, Hkv, D), generator=g).to(torch.bfloat16)
@@ -439,28 +441,102 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
                                     "config": {"tokens": T, "heads": f"{Hq}q/{Hkv}kv x {D}", "dtype": "bf16"}}}
 
 
+# ------------------------------------------------------------------ shared line pieces
+def load_workloads():
+    """The seeded workload generators (mini-sglang-mlx_b200/minisgl_b200/workloads.py, numpy only).
+
+    Loaded by file path, so the reference arm gets its batches without importing the
+    minisgl_b200 package (whose import loads the CUDA library).
+    """
+    import importlib.util
+
+    name = "_bench_workloads"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(name, ROOT / "mini-sglang-mlx_b200" / "minisgl_b200" / "workloads.py")
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def warmup_steps(args) -> int:
+    """Untimed warm-up steps, the same in both arms (at least 3)."""
+    return max(args.warmup, 3)
+
+
+def config2_config(W, world: int, B: int, sum_ctx: int, layers: int) -> dict:
+    """The `config` of the headline line (config 2), identical in both arms."""
+    c = W.CONFIG2
+    return {
+        "workload": "config2: batched paged decode step, Qwen3-0.6B attention x28 layers "
+                    "(16q/8kv/128, bf16, page 16, pool 262144 slots/layer, B=128/GPU, L~U[100,2048], "
+                    "fragmented pages); per layer fused RoPE+KV store + split-KV decode",
+        "global_batch": B * world, "seq_len": f"U[{c['lo']},{c['hi']}]", "parallelism": f"request-partitioned x{world}",
+        "l2": "inputs larger than L2 (each layer's ~560 MB KV working set > 126 MB L2)",
+        "sum_ctx_tokens_per_gpu": sum_ctx, "layers": layers,
+    }
+
+
+DECODE_PROFILE = ROOT / "profiles" / "decode_kernel_config2.md"
+DECODE_SOURCES = ("mini-sglang-mlx_b200/csrc/decode.cuh", "mini-sglang-mlx_b200/csrc/common.cuh")
+
+
+def decode_sources_digest() -> str:
+    """SHA-256 (first 16 hex digits) of the decode kernel's sources, in DECODE_SOURCES order."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for f in DECODE_SOURCES:
+        h.update((ROOT / f).read_bytes())
+    return h.hexdigest()[:16]
+
+
+def decode_traffic():
+    """DRAM bytes (read + write) per decode launch from the committed ncu summary.
+
+    profiles/decode_kernel_config2.md carries a line
+    ``traffic: <bytes> bytes per launch, decode sources <digest>``; the figure is
+    used only when <digest> is the digest of the sources being timed, so a kernel
+    change makes it null ("stale") instead of silently wrong.
+    """
+    import re
+
+    if not DECODE_PROFILE.exists():
+        return None, "no ncu summary committed"
+    m = re.search(r"traffic: (\d+) bytes per launch, decode sources ([0-9a-f]{16})", DECODE_PROFILE.read_text())
+    if not m:
+        return None, "ncu summary has no traffic line"
+    if m.group(2) != decode_sources_digest():
+        return None, f"stale: captured on decode sources {m.group(2)}, timed on {decode_sources_digest()}"
+    return int(m.group(1)), f"ncu capture of decode_kernel on config-2 layer 0, seed 0, decode sources {m.group(2)}"
+
+
 # ------------------------------------------------------------------ reference arm
 def run_reference(args):
+    """The reference arm: the CPU oracle port of the naive decode (the MLX CPU path cannot
+    run on this box). Rank 0 alone runs it; the minisgl_b200 package is never imported."""
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    from minisgl_b200 import workloads as W
-
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    W = load_workloads()
     c = W.CONFIG2
     pb = W.config2_batch(seed=args.seed)
-    steps = max(1, min(args.steps, 20))
-    warm = max(0, min(args.warmup, 3))
+    steps = args.steps
+    warm = warmup_steps(args)
     gbs, per_call, cores = cpu_sample(pb.lens, pb.page_table, pb.page_size, c["Hq"], c["Hkv"], c["D"],
                                       c["num_slots"], steps, warm, args.seed)
-    sample = (f"one layer of config 2 per step (B={pb.batch_size}, sum L={int(pb.lens.sum())}, bf16 pools, "
-              f"naive gather+mask+SDPA in fp32 on {cores} threads); {steps} timed steps")
+    sample = (f"each step is one of the 28 layers of a config-2 step (B={pb.batch_size}, "
+              f"sum L={int(pb.lens.sum())}, bf16 pools, naive gather+mask+SDPA in fp32 on {cores} threads); "
+              f"GB/s is the same rate for 1 or 28 layers; {steps} timed steps after {warm} warm-up")
     line = {
-        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": args.gpus,
+        "impl": "reference", "metric": METRIC, "value": round(gbs, 3), "unit": UNIT, "n_gpus": world,
         "steps": steps, "warmup": warm, "ms_per_step": round(per_call * 1e3, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": "config2: batched paged decode, 16q/8kv/128, page 16, B=128, L~U[100,2048]",
-                   "kind": "cpu oracle port (MLX CPU path unavailable on this box)"},
-        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample},
+        "config": config2_config(W, world, pb.batch_size, int(pb.lens.sum()), c["layers"]),
+        "cpu_baseline": {"value": round(gbs, 3), "unit": UNIT, "cores": cores, "kind": "port", "sample": sample,
+                         "note": "torch CPU restatement of attention/naive.py:36-60; MLX CPU unavailable on this box"},
         "e2e": {"value": round(gbs, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -542,7 +618,7 @@ def run_ours(args):
                     be.forward(q, k, v, l, batch)
 
     # ---------------- per-call decode timing for the roofline (eager launches, CUDA events)
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(warmup_steps(args)):
         step()
     torch.cuda.synchronize()
     for _ in range(args.steps):
@@ -554,7 +630,7 @@ def run_ours(args):
     g_dev = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g_dev):
         step()
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(warmup_steps(args)):
         g_dev.replay()
     torch.cuda.synchronize()
     if world > 1:
@@ -631,7 +707,7 @@ def run_ours(args):
         be.refresh_decode_metadata(meta, req_rows, req_lens)
         g_e2e.replay()
 
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(warmup_steps(args)):
         e2e_step()
     torch.cuda.synchronize()
     if world > 1:
@@ -661,7 +737,8 @@ def run_ours(args):
 
     peak, peak_kind = measured_peaks()
     achieved = dbytes / (dec_avg * 1e-3) / 1e9
-    launches_per_step = Lyr * (2 + (1 if meta.n_partials > 0 else 0))
+    traffic, traffic_src = decode_traffic()
+    launches_per_step = Lyr * 2  # fused RoPE + store, decode (split requests merge inside the decode launch)
 
     # free the config-2 pools and graphs before the long-context measurement
     del g_dev, g_e2e, kv, be, ctx, layers, q_all, kv_all, dev_q, dev_kv
@@ -683,26 +760,18 @@ def run_ours(args):
                              f"torch CPU naive gather+mask+SDPA; MLX CPU unavailable on this box"}
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+            "warmup": warmup_steps(args), "ms_per_step": round(ms, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {
-                "workload": "config2: batched paged decode step, Qwen3-0.6B attention x28 layers "
-                            "(16q/8kv/128, bf16, page 16, pool 262144 slots/layer, B=128/GPU, L~U[100,2048], "
-                            "fragmented pages); per layer fused RoPE+KV store + split-KV decode",
-                "global_batch": B * world, "seq_len": "U[100,2048]", "parallelism": f"request-partitioned x{world}",
-                "l2": "inputs larger than L2 (each layer's ~560 MB KV working set > 126 MB L2)",
-                "sum_ctx_tokens_per_gpu": int(pb.lens.sum()), "layers": Lyr,
-            },
+            "config": config2_config(W, world, B, int(pb.lens.sum()), Lyr),
             "roofline": {
-                "bound": "hbm", "kernel": "decode_kernel+decode_merge_kernel (one b2a_decode call)",
+                "bound": "hbm", "kernel": "decode_kernel (one b2a_decode call; split requests merged in-launch)",
                 "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                 "frac": round(achieved / peak, 4), "peak_kind": peak_kind,
                 "bytes_per_launch": dbytes, "avg_launch_ms": round(dec_avg, 5),
-                # dram__bytes_read.sum + dram__bytes_write.sum of decode_kernel from one ncu
-                # capture of this seed-0 workload's layer 0 (574.76 MB + 4.58 MB); the
-                # merge kernel's few MB of partials are not in it
-                "traffic": 579340000 if args.seed == 0 else None,
-                "traffic_source": "ncu --set full, decode_kernel, config-2 layer 0, seed 0 (merge kernel excluded)",
+                # dram__bytes_read.sum + dram__bytes_write.sum of one decode_kernel launch from the
+                # committed ncu summary, used only if it was captured on the decode sources timed here
+                "traffic": traffic if args.seed == 0 else None,
+                "traffic_source": traffic_src if args.seed == 0 else "ncu capture is of seed 0 only",
             },
             "e2e": {"value": round(e2e_value, 2), "unit": UNIT,
                     "h2d_bytes_per_step": int((host_q.numel() + host_kv.numel()) * 2 + meta_bytes),

@@ -145,6 +145,19 @@ int b2a_paged_decode(const void* q, const void* k_pool, const void* v_pool, int6
  *   merge_indptr (out)          : int32 [B + 1] CSR over partial slots
  * b2a_decode_num_ctas returns the persistent grid size the kernel wants on
  * the current device for this head shape (SM count x resident CTAs).
+ *
+ * b2a_decode runs the plan in ONE launch: the CTA that writes the last
+ * partial of a split request (found with a per-request int32 merge counter,
+ * an atomic count, never a wait) merges that request's partials.
+ * Workspace (b2a_decode_workspace_bytes(n_partials, Hq, D) bytes or more,
+ * 256-byte aligned): the merge counters (int32 [n_partials]) sit at its start
+ * and the fp32 partial rows at its end. Zero-fill a workspace once when it is
+ * allocated; every completed call leaves the counters at zero again, so a
+ * buffer can be reused by any number of calls with any n_partials (for one
+ * head shape). A segment whose request id is outside [0, B) or whose partial
+ * slot is outside its request's merge range (or past n_partials) is skipped
+ * and reported as device error 35 (b2a_device_error); such a call can leave
+ * counters set, so zero the workspace again before the next call.
  * ------------------------------------------------------------------------ */
 int b2a_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,
                     int page_size, int num_ctas, int32_t* cta_indptr, int32_t* segs,
@@ -203,15 +216,18 @@ int b2a_page_table_scatter(int32_t* page_table, int64_t table_rows, int64_t tabl
  * runs, for example an engine whose memory planner has given the device to
  * the KV pool, or a host that may only pass buffers it already owns.
  * Same arguments and results as b2a_decode without workspace/workspace_bytes.
- * The split partials live in an 8 MiB file-scope device array inside the
- * library, held by every GPU that loads it until the process exits; a plan
- * whose b2a_decode_workspace_bytes(n_partials, Hq, D) exceeds 8 MiB is
- * rejected with B2A_ERR_WORKSPACE. The first call on a device looks up that
- * array's device address (cudaGetSymbolAddress) with the device current; make
- * that first call before any stream capture. All calls share the array and it
- * keeps the last call's contents, so calls that overlap on the GPU (other
- * streams, other host threads) race; serialise them. Nothing in the array has
- * to start at zero.
+ * The split partials and merge counters live in an 8 MiB file-scope device
+ * array inside the library, held by every GPU that loads it until the process
+ * exits; a plan whose b2a_decode_workspace_bytes(n_partials, Hq, D) exceeds
+ * 8 MiB is rejected with B2A_ERR_WORKSPACE. Every call made outside stream
+ * capture looks up that array's device address (cudaGetSymbolAddress) with
+ * its device current, so a reset device or another current context is
+ * followed; a call made during capture reuses the address the last such call
+ * found, so make the first call on a device before any stream capture. All
+ * calls share the array and it keeps the last call's contents, so calls that
+ * overlap on the GPU (other streams, other host threads) race; serialise
+ * them. Each call clears the merge counters with a stream-ordered memset
+ * before its kernel; the partial rows are written before they are read.
  * ------------------------------------------------------------------------ */
 int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
                        const int32_t* kv_indices, int page_size, const int32_t* cta_indptr,
@@ -222,7 +238,7 @@ int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, in
 /* ------------------------------------------------------------------------
  * Ragged causal extend (prefill) attention over a paged prefix.
  * Replaces BaseAttnBackend._prepare_prefill/_forward_prefill
- * (python/minisgl_mlx/attention/base.py:107-142): request r owns query rows
+ * (python/minisgl_mlx/attention/base.py:70-105): request r owns query rows
  * [qo_indptr[r], qo_indptr[r+1]) (Lq rows) and Lkv pool tokens described by
  * its pages (the cached prefix followed by the rows just stored). Row i of r
  * attends keys j <= Lkv - Lq + i (bottom-right causal, mx.fast SDPA

@@ -2,6 +2,7 @@
 // kernel configuration and dispatch. Declarations and contracts live in
 // include/b200attn.h; each kernel file names the reference code it replaces.
 #include <algorithm>
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -455,11 +456,43 @@ int b2a_decode_num_ctas(int Hq, int Hkv, int D, int dtype, int* num_ctas) {
   return ok();
 }
 
+}  // extern "C"
+
+namespace {
+size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+// Split-partial rows of a decode call: acc [n, Hq, D] then (m, l) [n, Hq, 2], fp32.
+size_t decode_partial_bytes(int n_partials, int Hq, int D) {
+  return align256((size_t)n_partials * Hq * D * sizeof(float)) + (size_t)n_partials * Hq * 2 * sizeof(float);
+}
+
+// Workspace layout: the merge counters (int32 [n_partials]) at its START, the
+// partial rows at its END (256-byte aligned). With every call's counters at
+// the front and partials at the back, no call's partials ever overlap the
+// counters of another call made with a different n_partials on the same
+// buffer, so counters only ever hold counts (zero between calls).
+struct DecodeWs {
+  int32_t* tickets;
+  float* acc;
+  float* ml;
+};
+DecodeWs decode_ws_layout(void* ws, size_t ws_bytes, int n_partials, int Hq, int D) {
+  DecodeWs w;
+  uint8_t* base = reinterpret_cast<uint8_t*>(ws);
+  const size_t part = decode_partial_bytes(n_partials, Hq, D);
+  const size_t acc_off = (ws_bytes - part) & ~(size_t)255;
+  w.tickets = reinterpret_cast<int32_t*>(base);
+  w.acc = reinterpret_cast<float*>(base + acc_off);
+  w.ml = reinterpret_cast<float*>(base + acc_off + align256((size_t)n_partials * Hq * D * sizeof(float)));
+  return w;
+}
+}  // namespace
+
+extern "C" {
+
 size_t b2a_decode_workspace_bytes(int n_partials, int Hq, int D) {
   if (n_partials <= 0) return 0;
-  const size_t acc = (size_t)n_partials * Hq * D * sizeof(float);
-  const size_t ml = (size_t)n_partials * Hq * 2 * sizeof(float);
-  return ((acc + 255) & ~(size_t)255) + ml;
+  return align256((size_t)n_partials * sizeof(int32_t)) + decode_partial_bytes(n_partials, Hq, D);
 }
 
 static int decode_common(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
@@ -480,6 +513,7 @@ static int decode_common(const void* q, const void* k_pool, const void* v_pool, 
   if (es == 0 || dtype == B2A_DTYPE_F16) return fail(B2A_ERR_UNSUPPORTED, "decode dtype %d", dtype);
   DecodeCfg c;
   if (int rc = decode_config(Hq, Hkv, D, es, c)) return rc;
+  if (n_partials < 0) return fail(B2A_ERR_INVALID, "n_partials must be >= 0");
   const size_t need = b2a_decode_workspace_bytes(n_partials, Hq, D);
   if (n_partials > 0 && (!workspace || workspace_bytes < need || !merge_indptr))
     return fail(B2A_ERR_WORKSPACE, "workspace of %zu bytes needed, %zu given", need, workspace_bytes);
@@ -493,10 +527,18 @@ static int decode_common(const void* q, const void* k_pool, const void* v_pool, 
   a.kv_indptr = kv_indptr;
   a.cta_indptr = cta_indptr;
   a.segs = segs;
-  a.ws_acc = reinterpret_cast<float*>(workspace);
-  a.ws_ml = n_partials > 0 ? reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(workspace) +
-                                                      (((size_t)n_partials * Hq * D * 4 + 255) & ~(size_t)255))
-                           : nullptr;
+  a.merge_indptr = merge_indptr;
+  if (n_partials > 0) {
+    const DecodeWs w = decode_ws_layout(workspace, workspace_bytes, n_partials, Hq, D);
+    a.tickets = w.tickets;
+    a.ws_acc = w.acc;
+    a.ws_ml = w.ml;
+  } else {
+    a.tickets = nullptr;
+    a.ws_acc = a.ws_ml = nullptr;
+  }
+  a.B = B;
+  a.n_partials = n_partials;
   a.out = out;
   a.page_log2 = plog;
   a.Hq = Hq;
@@ -516,20 +558,12 @@ static int decode_common(const void* q, const void* k_pool, const void* v_pool, 
       constexpr int Dc = decltype(dc)::value;
       return with_g<Dc>(G, [&](auto gc) {
         constexpr int Gc = decltype(gc)::value;
-        int r;
+        // split requests are merged inside the decode launch (merge tickets)
         if constexpr (Dc <= 128 && Gc <= 4) {
-          r = c.NCW == 16 ? decode_launch<Tt, Dc, Gc, 16>(a, c, grid, st) : decode_launch<Tt, Dc, Gc, 8>(a, c, grid, st);
+          return c.NCW == 16 ? decode_launch<Tt, Dc, Gc, 16>(a, c, grid, st) : decode_launch<Tt, Dc, Gc, 8>(a, c, grid, st);
         } else {
-          r = decode_launch<Tt, Dc, Gc, 8>(a, c, grid, st);
+          return decode_launch<Tt, Dc, Gc, 8>(a, c, grid, st);
         }
-        if (r) return r;
-        if (n_partials > 0) {
-          const int blocks = (B * Hq + 3) / 4;
-          launch_pdl(b2a::decode_merge_kernel<Tt, Dc>, dim3(blocks), dim3(128), 0, st, (const float*)a.ws_acc,
-                     (const float*)a.ws_ml, merge_indptr, out, B, Hq);
-          return check_launch("decode_merge_kernel");
-        }
-        return ok();
       });
     });
   });
@@ -562,16 +596,23 @@ int b2a_decode(const void* q, const void* k_pool, const void* v_pool, int64_t nu
 // decode: an engine whose memory planner has handed the whole device to the
 // KV pool, or a host that is only allowed to pass pointers it already owns
 // (pre-registered buffers, a foreign framework's tensors). For them the
-// split-KV partials live in this file-scope device array instead of a
-// caller-provided workspace. The array is part of the library image, so every
-// GPU that loads the library keeps it until the process exits.
+// split-KV partials and merge counters live in this file-scope device array
+// instead of a caller-provided workspace. The array is part of the library
+// image, so every GPU that loads the library keeps it until the process exits.
 namespace {
 
 constexpr size_t kNoAllocScratchBytes = (size_t)8 << 20;  // 8 MiB of split partials per device
 __device__ __align__(256) uint8_t g_decode_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
-void* g_decode_scratch_addr[kMaxDevices] = {};  // device address of g_decode_scratch, per device
+// Device address of g_decode_scratch, per device ordinal. Written and read
+// atomically, so first calls from several host threads are well defined (they
+// all store the same address). It is refreshed by every call made outside
+// stream capture: after cudaDeviceReset, or with another context current, the
+// module is loaded again and the array may move, so a cached address is only
+// trusted while a capture is in progress (capture cannot follow a reset
+// without a non-captured call, which refreshes it).
+std::atomic<void*> g_decode_scratch_addr[kMaxDevices];
 
 }  // namespace
 
@@ -581,6 +622,7 @@ extern "C" int b2a_decode_noalloc(const void* q, const void* k_pool, const void*
                                   int B, int Hq, int Hkv, int D, float scale, void* out, int dtype, void* stream) {
   if (!cta_indptr || !segs || num_ctas <= 0) return fail(B2A_ERR_INVALID, "decode plan missing (cta_indptr/segs)");
   if (!aligned(segs, 16)) return fail(B2A_ERR_INVALID, "segs must be 16-byte aligned (read as int4)");
+  if (n_partials < 0) return fail(B2A_ERR_INVALID, "n_partials must be >= 0");
   const size_t need = b2a_decode_workspace_bytes(n_partials, Hq, D);
   if (need > kNoAllocScratchBytes)
     return fail(B2A_ERR_WORKSPACE,
@@ -591,20 +633,35 @@ extern "C" int b2a_decode_noalloc(const void* q, const void* k_pool, const void*
   cudaError_t e = cudaGetDevice(&dev);
   if (e != cudaSuccess || dev < 0 || dev >= kMaxDevices)
     return fail(B2A_ERR_CUDA, "b2a_decode_noalloc: no usable current device (%s)", cudaGetErrorString(e));
-  if (!g_decode_scratch_addr[dev]) {
-    // One-time set-up on this device (the device is current here): the host
-    // symbol is only a stand-in, the kernel needs the device address.
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_decode_scratch);
-    if (e != cudaSuccess || !p)
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+  e = cudaStreamIsCapturing(st, &cap);
+  if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "b2a_decode_noalloc: %s", cudaGetErrorString(e));
+  void* scratch = nullptr;
+  if (cap == cudaStreamCaptureStatusNone) {
+    // Set-up on this device, with the device current: the host-side symbol is
+    // only a stand-in, the kernel needs the array's device address.
+    e = cudaGetSymbolAddress(&scratch, g_decode_scratch);
+    if (e != cudaSuccess || !scratch)
       return fail(B2A_ERR_CUDA, "b2a_decode_noalloc: cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
-    g_decode_scratch_addr[dev] = p;
+    g_decode_scratch_addr[dev].store(scratch, std::memory_order_release);
+  } else {
+    scratch = g_decode_scratch_addr[dev].load(std::memory_order_acquire);
+    if (!scratch)
+      return fail(B2A_ERR_INVALID,
+                  "b2a_decode_noalloc: the first call on a device must come before any stream capture");
   }
-  // The merge kernel reads only partial rows the decode kernel wrote in the
-  // same call, so nothing in the scratch has to start at zero.
+  // The array keeps the last call's contents. The merge counters at its start
+  // must be zero: a completed call leaves them so, but a call cut short by a
+  // device error may not, so they are cleared here (a memset, no allocation).
+  // Partial rows need no clearing: each is written before it is read.
+  if (n_partials > 0) {
+    e = cudaMemsetAsync(scratch, 0, (size_t)n_partials * sizeof(int32_t), st);
+    if (e != cudaSuccess) return fail(B2A_ERR_CUDA, "b2a_decode_noalloc: clear counters: %s", cudaGetErrorString(e));
+  }
   return decode_common(q, k_pool, v_pool, num_slots, kv_indices, nullptr, page_size, cta_indptr, segs, num_ctas,
-                       merge_indptr, n_partials, B, Hq, Hkv, D, scale, g_decode_scratch_addr[dev],
-                       kNoAllocScratchBytes, out, dtype, stream);
+                       merge_indptr, n_partials, B, Hq, Hkv, D, scale, scratch, kNoAllocScratchBytes, out, dtype,
+                       stream);
 }
 
 extern "C" {

@@ -28,6 +28,7 @@ enum WatchdogCode : int {
   kWdTileTooLarge = 33,  // a work tile larger than the kernel's tile: clamped
   kWdBadSlot = 32,  // a page id / slot outside the pool: access skipped
   kWdMetaOverflow = 34,  // device metadata: a row, length or entry outside its buffer: skipped
+  kWdBadPlan = 35,       // decode plan: a request id or partial slot outside its bounds: segment skipped
 };
 
 __device__ __forceinline__ void watchdog_set(int code) { atomicCAS(&g_watchdog, 0, code); }

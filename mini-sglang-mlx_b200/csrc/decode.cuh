@@ -12,8 +12,12 @@
 //     ring, completion tracked by mbarriers (one producer warp).
 //   * Grid = persistent CTAs, each owning a contiguous, equal share of the
 //     concatenated page stream of the batch (host plan). A request cut by a
-//     share boundary produces partial (m, l, acc) rows that a merge kernel
-//     combines; requests inside a share are written directly.
+//     share boundary produces partial (m, l, acc) rows; requests inside a
+//     share are written directly. Each split request has a merge ticket (an
+//     int32 counter in the workspace): a CTA that has written one of its
+//     partials takes a ticket, and the CTA that takes the last one merges all
+//     of that request's partials and re-arms the counter to zero. No CTA ever
+//     waits for another, and no separate merge launch follows.
 //   * NCW consumer warps (16 when shared memory allows, else 8); warp w
 //     serves kv head w / WPH and every WPH-th group of TG tokens of a stage,
 //     so two or more groups are in flight per head. Lane = D/32 features. The
@@ -39,10 +43,14 @@ struct DecodeArgs {
   const int32_t* kv_indptr;   // direct mode: token CSR (page_size 1)
   const int32_t* cta_indptr;  // plan mode: CSR over segs; NULL = direct mode
   const int32_t* segs;        // int4 {request, first page idx, n_tokens, out_slot}
+  const int32_t* merge_indptr;  // [B + 1] CSR over partial slots (plan mode)
   float* ws_acc;              // [n_partials, Hq, D]
   float* ws_ml;               // [n_partials, Hq, 2]
+  int32_t* tickets;           // [n_partials] merge counters, indexed by a request's first partial slot
   void* out;                  // [B, Hq, D]
   int64_t num_slots;
+  int B;           // requests (bounds of the plan's request ids)
+  int n_partials;  // partial slots the workspace holds (bounds of the plan's slots)
   int page_log2;
   int Hq, Hkv;
   float qscale;  // softmax scale * log2(e)
@@ -56,7 +64,7 @@ struct DecodeArgs {
 
 struct DecodeSmem {
   // byte offsets inside the dynamic shared memory block
-  uint32_t bars, pbuf, cbuf, abort_flag, total;
+  uint32_t bars, pbuf, cbuf, abort_flag, last_flag, total;
 };
 
 __host__ __device__ inline DecodeSmem decode_smem_layout(int NSTAGE, uint32_t stage_bytes, int NCW, int WPH,
@@ -72,6 +80,8 @@ __host__ __device__ inline DecodeSmem decode_smem_layout(int NSTAGE, uint32_t st
   L.cbuf = off;
   if (WPH > 1) off += (uint32_t)NCW * (uint32_t)G * (uint32_t)(D + 2) * 4u;
   L.abort_flag = off;
+  off += 16;
+  L.last_flag = off;
   off += 16;
   L.total = off;
   return L;
@@ -91,6 +101,17 @@ __device__ __forceinline__ void decode_get_seg(const DecodeArgs& a, int idx, int
     ntok = a.kv_indptr[b + 1] - page_begin;
     slot = -1;
   }
+}
+
+// A segment is used only if its request id is in [0, B) and, when it writes a
+// partial, its slot lies in its request's merge range inside the workspace.
+// Producer and consumers decide identically, so a rejected segment is skipped
+// by both (no stage is issued or awaited for it) and reported as kWdBadPlan.
+__device__ __forceinline__ bool decode_seg_ok(const DecodeArgs& a, int b, int slot) {
+  if (b < 0 || b >= a.B) return false;
+  if (slot < 0) return true;
+  const int p0 = a.merge_indptr[b], p1 = a.merge_indptr[b + 1];
+  return p0 >= 0 && p0 <= slot && slot < p1 && p1 <= a.n_partials;
 }
 
 template <int G>
@@ -237,6 +258,43 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* 
   __syncwarp();
 }
 
+// Combine the partial rows of request b (slots [p0, p1)), written by this and
+// other CTAs of the same launch: consumer warp w takes query heads w, w + NCW, ...
+// The rows are read through L2 (ld.global.cg): another SM wrote them, and this
+// SM's L1 may still hold lines of the same workspace from an earlier launch.
+template <typename T, int D>
+__device__ __forceinline__ void decode_merge_request(const DecodeArgs& a, int b, int p0, int p1, int warp,
+                                                     int lane) {
+  constexpr int EPT = D / 32;
+  const int Hq = a.Hq;
+  for (int qh = warp; qh < Hq; qh += a.NCW) {
+    float M = kNegInf;
+    for (int p = p0; p < p1; ++p) M = fmaxf(M, __ldcg(a.ws_ml + ((size_t)p * Hq + qh) * 2));
+    float Lsum = 0.f, acc[EPT];
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) acc[e] = 0.f;
+    for (int p = p0; p < p1; ++p) {
+      const float m = __ldcg(a.ws_ml + ((size_t)p * Hq + qh) * 2);
+      const float l = __ldcg(a.ws_ml + ((size_t)p * Hq + qh) * 2 + 1);
+      const float w = (m == kNegInf) ? 0.f : exp2f(m - M);
+      Lsum += l * w;
+      const float* src = a.ws_acc + ((size_t)p * Hq + qh) * D + lane * EPT;
+#pragma unroll
+      for (int e = 0; e < EPT; e += 4) {
+        const float4 o = __ldcg(reinterpret_cast<const float4*>(src + e));
+        acc[e + 0] = fmaf(w, o.x, acc[e + 0]);
+        acc[e + 1] = fmaf(w, o.y, acc[e + 1]);
+        acc[e + 2] = fmaf(w, o.z, acc[e + 2]);
+        acc[e + 3] = fmaf(w, o.w, acc[e + 3]);
+      }
+    }
+    const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
+#pragma unroll
+    for (int e = 0; e < EPT; ++e) acc[e] *= inv;
+    store_vec<T, EPT>(reinterpret_cast<T*>(a.out) + ((size_t)b * Hq + qh) * D + lane * EPT, acc);
+  }
+}
+
 template <typename T, int D, int G, int NCW>
 __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeArgs a) {
   pdl_wait_then_release();
@@ -287,6 +345,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
     for (int si = seg0; si < seg1 && ok; ++si) {
       int b, pbeg, ntok, slot;
       decode_get_seg(a, si, b, pbeg, ntok, slot);
+      if (!decode_seg_ok(a, b, slot)) continue;  // the consumers skip it too (and report it)
       for (int tok = 0; tok < ntok; tok += TS) {
         if (!__all_sync(FULL, *s_abort == 0)) {
           ok = false;
@@ -382,11 +441,16 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
   const int sub = warp - h * a.WPH;
   float* pb = reinterpret_cast<float*>(smem + L.pbuf) + warp * 32;
   float* cbuf = reinterpret_cast<float*>(smem + L.cbuf);
+  volatile int* s_last = reinterpret_cast<volatile int*>(smem + L.last_flag);
   const T* qbase = reinterpret_cast<const T*>(a.q);
   int ctr = 0;
   for (int si = seg0; si < seg1; ++si) {
     int b, pbeg, ntok, slot;
     decode_get_seg(a, si, b, pbeg, ntok, slot);
+    if (!decode_seg_ok(a, b, slot)) {
+      if (threadIdx.x == 0) watchdog_set(kWdBadPlan);
+      continue;
+    }
     uint64_t qv2[G][EPT / 2], acc2[G][EPT / 2];
 #pragma unroll
     for (int g = 0; g < G; ++g) {
@@ -488,46 +552,30 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
             a.ws_ml[((size_t)slot * a.Hq + h * G + g) * 2 + 1] = lg[g];
           }
         }
+        __threadfence();  // publish this warp's partial rows at GPU scope before the ticket
       }
     }
-    if (a.WPH > 1) named_bar_sync(1, a.NCW * 32);
+    if (slot >= 0) {
+      // Merge ticket of request b (every consumer warp sees the same slot). An
+      // aborted CTA still gets here for each of its segments, so a counter
+      // always reaches its request's partial count and is re-armed.
+      named_bar_sync(1, a.NCW * 32);
+      const int p0 = a.merge_indptr[b], p1 = a.merge_indptr[b + 1];
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&a.tickets[p0], 1);
+        const bool last = prev == p1 - p0 - 1;
+        if (last) a.tickets[p0] = 0;  // every partial has arrived: re-arm for the next call
+        *s_last = last ? 1 : 0;
+      }
+      named_bar_sync(1, a.NCW * 32);
+      if (*s_last) {
+        __threadfence();
+        decode_merge_request<T, D>(a, b, p0, p1, warp, lane);
+      }
+    } else if (a.WPH > 1) {
+      named_bar_sync(1, a.NCW * 32);
+    }
   }
-}
-
-// Combine the partial rows of requests that were cut across CTAs.
-template <typename T, int D>
-__global__ void __launch_bounds__(128) decode_merge_kernel(const float* __restrict__ ws_acc,
-                                                           const float* __restrict__ ws_ml,
-                                                           const int32_t* __restrict__ merge_indptr, void* out,
-                                                           int B, int Hq) {
-  pdl_wait_then_release();
-  constexpr int EPT = D / 32;
-  const int lane = threadIdx.x & 31;
-  const int idx = blockIdx.x * 4 + (threadIdx.x >> 5);
-  if (idx >= B * Hq) return;
-  const int b = idx / Hq;
-  const int qh = idx - b * Hq;
-  const int p0 = merge_indptr[b], p1 = merge_indptr[b + 1];
-  if (p1 <= p0) return;
-  float M = kNegInf;
-  for (int p = p0; p < p1; ++p) M = fmaxf(M, ws_ml[((size_t)p * Hq + qh) * 2]);
-  float Lsum = 0.f, acc[EPT];
-#pragma unroll
-  for (int e = 0; e < EPT; ++e) acc[e] = 0.f;
-  for (int p = p0; p < p1; ++p) {
-    const float m = ws_ml[((size_t)p * Hq + qh) * 2];
-    const float l = ws_ml[((size_t)p * Hq + qh) * 2 + 1];
-    const float w = (m == kNegInf) ? 0.f : exp2f(m - M);
-    Lsum += l * w;
-    float o[EPT];
-    load_vec<float, EPT>(ws_acc + ((size_t)p * Hq + qh) * D + lane * EPT, o);
-#pragma unroll
-    for (int e = 0; e < EPT; ++e) acc[e] = fmaf(w, o[e], acc[e]);
-  }
-  const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
-#pragma unroll
-  for (int e = 0; e < EPT; ++e) acc[e] *= inv;
-  store_vec<T, EPT>(reinterpret_cast<T*>(out) + ((size_t)b * Hq + qh) * D + lane * EPT, acc);
 }
 
 }  // namespace b2a

@@ -1,6 +1,6 @@
 // Ragged causal extend (prefill) attention, SIMT fp32-accumulating kernel.
 //
-// Reference: python/minisgl_mlx/attention/base.py:107-142. Request r owns
+// Reference: python/minisgl_mlx/attention/base.py:70-105. Request r owns
 // query rows [qo_indptr[r], qo_indptr[r+1]) (Lq of them) and Lkv pool tokens
 // (prefix + the rows just stored); row i sees keys j <= Lkv - Lq + i
 // (bottom-right causal). This kernel is the exact-fp32 path (parity 1e-5) and

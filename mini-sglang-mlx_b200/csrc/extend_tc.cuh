@@ -1,6 +1,6 @@
 // Ragged causal extend attention on 5th-generation tensor cores (sm_100a).
 //
-// Reference: python/minisgl_mlx/attention/base.py:107-142 (per-request SDPA,
+// Reference: python/minisgl_mlx/attention/base.py:70-105 (per-request SDPA,
 // bottom-right causal). Same contract as extend_simt.cuh; this is the
 // bf16 / head_dim 128 / page_size % 16 == 0 path.
 //

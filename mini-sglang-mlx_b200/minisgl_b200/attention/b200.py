@@ -5,10 +5,10 @@ Drop-in for the reference's backends (python/minisgl_mlx/attention/
 same ``prepare_metadata`` / ``forward`` / ``prepare_decode`` /
 ``forward_decode`` contract, computed by the CUDA kernels of libb200attn.so:
 
-* decode  -> ``b2a_decode``: persistent split-KV paged decode + merge
-  (replaces metal.py:112-162 and naive.py:36-60)
+* decode  -> ``b2a_decode``: persistent split-KV paged decode; split requests
+  are merged inside the same launch (replaces metal.py:112-162 and naive.py:36-60)
 * prefill -> ``b2a_extend``: ragged causal extend over the paged prefix
-  (replaces base.py:107-142)
+  (replaces base.py:70-105)
 
 There is no CPU or library fallback: without the CUDA library or a GPU the
 backend refuses to construct.
@@ -105,8 +105,10 @@ class B200AttnBackend(BaseAttnBackend):
         return self._page_size if self._page_size is not None else _page_size()
 
     def _workspace_for(self, nbytes: int) -> torch.Tensor:
+        # zero-filled once: the merge counters at its start must be zero before the
+        # first decode call, and every call leaves them at zero again
         if self._workspace.numel() < nbytes:
-            self._workspace = torch.empty(max(nbytes, 2 * self._workspace.numel()), dtype=torch.uint8,
+            self._workspace = torch.zeros(max(nbytes, 2 * self._workspace.numel()), dtype=torch.uint8,
                                           device=self.device)
         return self._workspace
 
@@ -159,7 +161,7 @@ class B200AttnBackend(BaseAttnBackend):
         dev, nc = self.device, self.num_ctas
         cap = batch_size + nc
         i32 = dict(dtype=torch.int32, device=dev)
-        ws = torch.empty(nat.decode_workspace_bytes(cap, self.Hq, self.D), dtype=torch.uint8, device=dev)
+        ws = torch.zeros(nat.decode_workspace_bytes(cap, self.Hq, self.D), dtype=torch.uint8, device=dev)
         return B200DecodeMetadata(
             kv_indptr=torch.zeros(batch_size + 1, **i32), kv_indices=torch.zeros(max(max_pages, 1), **i32),
             kv_last_page_len=torch.zeros(batch_size, **i32), cta_indptr=torch.zeros(nc + 1, **i32),

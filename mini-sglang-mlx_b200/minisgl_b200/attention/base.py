@@ -1,6 +1,6 @@
 """Attention backend interface and host-side metadata builders.
 
-Mirrors python/minisgl_mlx/attention/base.py:69-120: ``prepare_metadata(batch)``
+Mirrors python/minisgl_mlx/attention/base.py:49-105: ``prepare_metadata(batch)``
 runs on the host before the forward and stores the per-batch indices in
 ``batch.attn_metadata``; ``forward(q, k, v, layer_id, batch)`` dispatches on
 the batch phase. The prefill metadata keeps the reference's ``last_indices``

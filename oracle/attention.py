@@ -12,14 +12,15 @@ project):
   naive_prepare_decode      python/minisgl_mlx/attention/naive.py:36-48
   naive_forward_decode      python/minisgl_mlx/attention/naive.py:50-60
   metal_prepare_decode      python/minisgl_mlx/attention/metal.py:145-152
-  prepare_prefill           python/minisgl_mlx/attention/base.py:107-120
-  forward_prefill           python/minisgl_mlx/attention/base.py:122-142
+  prepare_prefill           python/minisgl_mlx/attention/base.py:70-83
+  forward_prefill           python/minisgl_mlx/attention/base.py:85-105
+  forward_prefill_torch     the same, pool branch, torch BLAS on the CPU (benchmark-sized batches)
   rope                      python/minisgl_mlx/layers.py:45-56 (mx.fast.rope, traditional=False)
   store_kv                  python/minisgl_mlx/kvcache/pool.py:47-50
   attention_layer           python/minisgl_mlx/layers.py:103-111
   sdpa                      mx.fast.scaled_dot_product_attention semantics as the
-                            reference calls it (attention/base.py:134-140,
-                            attention/naive.py:195-201): softmax(scale q k^T + mask) v,
+                            reference calls it (attention/base.py:97-103,
+                            attention/naive.py:53-59): softmax(scale q k^T + mask) v,
                             GQA by head grouping, boolean mask True = keep,
                             mask="causal" aligned to the bottom-right corner.
 
@@ -151,7 +152,7 @@ class PrefillMeta:
 
 def prepare_prefill(page_table: np.ndarray, table_idx: Sequence[int], cached_len: Sequence[int],
                     device_len: Sequence[int]) -> PrefillMeta:
-    """attention/base.py:107-120."""
+    """attention/base.py:70-83."""
     extend = [d - c for c, d in zip(cached_len, device_len)]
     q_offsets = np.concatenate([[0], np.cumsum(extend)]).astype(np.int64).tolist()
     kv_indices: List[Optional[np.ndarray]] = []
@@ -163,7 +164,7 @@ def prepare_prefill(page_table: np.ndarray, table_idx: Sequence[int], cached_len
 
 def forward_prefill(q: np.ndarray, k: np.ndarray, v: np.ndarray, k_pool: np.ndarray, v_pool: np.ndarray,
                     meta: PrefillMeta, scale: float, acc=np.float64) -> np.ndarray:
-    """attention/base.py:122-142: one SDPA per request, causal (bottom-right) when Lq > 1."""
+    """attention/base.py:85-105: one SDPA per request, causal (bottom-right) when Lq > 1."""
     outs = []
     for i, kv_idx in enumerate(meta.kv_indices):
         s, e = meta.q_offsets[i], meta.q_offsets[i + 1]
@@ -176,6 +177,44 @@ def forward_prefill(q: np.ndarray, k: np.ndarray, v: np.ndarray, k_pool: np.ndar
                   scale, causal=(e - s) > 1, acc=acc)
         outs.append(oi[0].transpose(1, 0, 2))
     return outs[0] if len(outs) == 1 else np.concatenate(outs, axis=0)
+
+
+def forward_prefill_torch(q, k_pool, v_pool, q_offsets: Sequence[int], kv_indices: List[np.ndarray], scale: float,
+                          dtype=None):
+    """attention/base.py:85-105 with every request reading its keys from the pool, in torch on the CPU.
+
+    The same arithmetic as ``forward_prefill`` (per-request SDPA, bottom-right causal when
+    Lq > 1, GQA by head grouping), written with BLAS matmuls so that batches of the
+    benchmark's size (thousands of query rows over thousands of keys) finish in seconds.
+    q [T, Hq, D], pools [N, Hkv, D] (torch CPU tensors, any float dtype); the math runs in
+    ``dtype`` (default float64). Returns [T, Hq, D] in ``dtype``.
+    """
+    import torch
+
+    dtype = dtype or torch.float64
+    T, Hq, D = q.shape
+    Hkv = k_pool.shape[1]
+    G = Hq // Hkv
+    out = torch.empty((T, Hq, D), dtype=dtype)
+    for i, idx in enumerate(kv_indices):
+        s0, s1 = int(q_offsets[i]), int(q_offsets[i + 1])
+        Lq = s1 - s0
+        if Lq == 0:
+            continue
+        sel = torch.from_numpy(np.asarray(idx, dtype=np.int64))
+        kr = k_pool[sel].to(dtype).permute(1, 0, 2)  # [Hkv, Lkv, D]
+        vr = v_pool[sel].to(dtype).permute(1, 0, 2)
+        Lkv = kr.shape[1]
+        qr = q[s0:s1].to(dtype).reshape(Lq, Hkv, G, D).permute(1, 2, 0, 3).reshape(Hkv, G * Lq, D)
+        sc = torch.matmul(qr, kr.transpose(1, 2)) * scale  # [Hkv, G*Lq, Lkv]
+        if Lq > 1:
+            row = torch.arange(Lq).repeat(G)  # query row of each (g, i) line
+            keep = torch.arange(Lkv)[None, :] <= (row[:, None] + (Lkv - Lq))
+            sc.masked_fill_(~keep[None], float("-inf"))
+        p = torch.softmax(sc, dim=-1)
+        o = torch.matmul(p, vr)  # [Hkv, G*Lq, D]
+        out[s0:s1] = o.reshape(Hkv, G, Lq, D).permute(2, 0, 1, 3).reshape(Lq, Hq, D)
+    return out
 
 
 # --------------------------------------------------------------------------- rope + store

@@ -5,10 +5,12 @@ from the reference checkout without importing it (mlx is not installed), writes
 it to oracle/_ref/paged_decode_body.inc (git-ignored, never committed) and
 compiles oracle/metal_ref/metal_shim.cpp around it with g++.
 
-    python oracle/metal_ref/build.py [--reference /path/to/mini-sglang-mlx]
+    python oracle/metal_ref/build.py --reference /path/to/mini-sglang-mlx
+    MINISGL_REFERENCE=/path/to/mini-sglang-mlx python oracle/metal_ref/build.py
 
-On a host without the reference checkout the prebuilt library (if any) is
-used as is.
+The checkout is named only by --reference or the MINISGL_REFERENCE
+environment variable. Without one (e.g. on a GPU host that has no checkout)
+the prebuilt library, if any, is used as is.
 """
 
 from __future__ import annotations
@@ -24,7 +26,6 @@ HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
 OUT = ROOT / "oracle" / "_ref"
 LIB = OUT / "libmetal_ref.so"
-DEFAULT_REF = Path(os.environ.get("MINISGL_REFERENCE", "/root/reference"))
 KERNEL_FILE = Path("python/minisgl_mlx/attention/metal.py")
 
 
@@ -36,9 +37,14 @@ def extract_body(reference: Path) -> str:
     raise RuntimeError(f"_PAGED_DECODE_SOURCE not found in {reference / KERNEL_FILE}")
 
 
+def default_reference() -> Path | None:
+    env = os.environ.get("MINISGL_REFERENCE")
+    return Path(env) if env else None
+
+
 def build(reference: Path | None = None, quiet: bool = False) -> Path | None:
-    reference = reference or DEFAULT_REF
-    if not (reference / KERNEL_FILE).exists():
+    reference = reference or default_reference()
+    if reference is None or not (reference / KERNEL_FILE).exists():
         return LIB if LIB.exists() else None
     OUT.mkdir(parents=True, exist_ok=True)
     body = extract_body(reference)

@@ -57,3 +57,21 @@ def test_reference_arm_under_two_ranks_prints_once():
     lines = [l for l in out.stdout.splitlines() if l.startswith("{")]
     assert len(lines) == 1  # rank 0 alone runs and prints; rank 1 exits without work
     _check_line(json.loads(lines[0]), 2)
+
+
+def test_reference_arm_never_loads_the_product_library():
+    """The reference arm times the CPU port only: the minisgl_b200 package (whose import
+    loads libb200attn.so) is never imported, and the library is not mapped."""
+    code = (
+        "import runpy, sys\n"
+        "sys.argv = ['bench.py', '--impl', 'reference', '--steps', '1', '--warmup', '0']\n"
+        "runpy.run_path('bench.py', run_name='__main__')\n"
+        "maps = open('/proc/self/maps').read()\n"
+        "print('PKG', any(m == 'minisgl_b200' or m.startswith('minisgl_b200.') for m in sys.modules))\n"
+        "print('LIB', 'libb200attn' in maps)\n"
+    )
+    out = subprocess.run([sys.executable, "-c", code], capture_output=True, text=True, timeout=600, cwd=ROOT)
+    assert out.returncode == 0, out.stderr[-2000:]
+    assert "PKG False" in out.stdout and "LIB False" in out.stdout, out.stdout[-500:]
+    line = json.loads([l for l in out.stdout.splitlines() if l.startswith("{")][0])
+    assert line["warmup"] >= 3  # the same warm-up rule as the GPU arm

@@ -178,6 +178,46 @@ def test_long_context_decode_qwen3_8b_shape(num_ctas):
     assert out <= TOL["bfloat16"], out
 
 
+def test_config5_decode_with_131072_token_request_and_200_partials():
+    """Config 5 (Qwen3-8B attention 32q/8kv/128, bf16, page 16, contexts log-uniform in
+    [1024, 131072]): the first 24 requests of the benchmark's seeded lengths with request 0
+    set to the 131,072-token maximum, planned over 296 CTAs so that more than 200 split
+    partials are written and merged. Oracle: the reference's per-request SDPA
+    (tests/test_attention.py:10-16 form) in float32 torch on the CPU."""
+    import torch
+
+    from minisgl_b200 import MHAKVCache
+    from minisgl_b200.attention import B200AttnBackend
+
+    lens = W.config5_lens(seed=0)[:24].copy()
+    lens[0] = 131072
+    rng = np.random.default_rng(12)
+    P, Hq, Hkv, D = 16, 32, 8, 128
+    pages = int(((lens + P - 1) // P).sum())
+    pb = W.allocate_pages(lens, (pages + 64) * P, P, rng)
+    gen = torch.Generator(device="cuda").manual_seed(12)
+    kv = MHAKVCache(1, pb.num_slots, Hkv, D, torch.bfloat16)
+    kv.k[0].normal_(generator=gen)
+    kv.v[0].normal_(generator=gen)
+    q = torch.randn((len(lens), Hq, D), device="cuda", generator=gen).to(torch.bfloat16)
+    be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=P)
+    meta = be.decode_metadata_from_lens(pb.rows, pb.lens, num_ctas=296)
+    assert meta.n_partials >= 200, meta.n_partials
+    out = be.forward_decode(q, 0, meta).float().cpu()
+    torch.cuda.synchronize()
+    kh, vh, qh = kv.k[0].cpu(), kv.v[0].cpu(), q.float().cpu()
+    G = Hq // Hkv
+    worst = 0.0
+    for b, L in enumerate(lens.tolist()):
+        sel = torch.from_numpy(pb.page_table[b, :L].astype(np.int64))
+        k = kh[sel].float().permute(1, 0, 2)  # [Hkv, L, D]
+        v = vh[sel].float().permute(1, 0, 2)
+        s = torch.matmul(qh[b].view(Hkv, G, D), k.transpose(1, 2)) * D ** -0.5
+        o = torch.matmul(torch.softmax(s, dim=-1), v).reshape(Hq, D)
+        worst = max(worst, float((out[b] - o).abs().max()))
+    assert worst <= TOL["bfloat16"], worst
+
+
 def _run_backend_decode_ref(pb, Hq, Hkv, D, dtype, num_ctas):
     import torch
 

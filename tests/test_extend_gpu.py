@@ -1,6 +1,6 @@
 """GPU parity of ragged causal extend (prefill) attention against the oracle.
 
-The oracle is the reference's shared prefill (attention/base.py:107-142): per
+The oracle is the reference's shared prefill (attention/base.py:70-105): per
 request SDPA, fresh k/v when nothing is cached, the pool rows of
 page_table[row, :device_len] otherwise, causal bottom-right when Lq > 1.
 """
@@ -80,6 +80,40 @@ def test_extend_config3_shapes(dtype):
     out, ref = _run_extend(eb, 16, 8, 128, dtype, seed=4)
     err = max_abs(out, ref)
     assert err <= TOL[dtype], err
+
+
+@pytest.mark.parametrize("P", [16, 1])
+def test_extend_config3_full_benchmark_batch(P):
+    """The whole config-3 batch the benchmark times (W.config3_batch(seed=0): 32 requests,
+    ~9.1 k query rows, prefixes up to 4096; page 16 runs the tcgen05 kernel directly, page 1
+    the page packer first). Oracle: the reference's prefill (attention/base.py:85-105) in
+    float64 torch BLAS on the CPU, all rows compared."""
+    import torch
+
+    from minisgl_b200 import MHAKVCache
+    from minisgl_b200.attention import B200AttnBackend
+
+    eb = W.config3_batch(seed=0, page_size=P)
+    pb = eb.paged
+    assert pb.batch_size == 32
+    Hq, Hkv, D = 16, 8, 128
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    kv = MHAKVCache(1, pb.num_slots, Hkv, D, torch.bfloat16)
+    kv.k[0].normal_(generator=gen)
+    kv.v[0].normal_(generator=gen)
+    T = int(eb.extend.sum())
+    q = torch.randn((T, Hq, D), device="cuda", generator=gen).to(torch.bfloat16)
+    be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=P)
+    meta = be.extend_metadata_from_lens(pb.rows, pb.lens, eb.extend)
+    assert (meta.pack is not None) == (P == 1)
+    out = be._forward_prefill(q, None, None, 0, meta).float().cpu()
+    torch.cuda.synchronize()
+    idx = [pb.page_table[b, : int(pb.lens[b])] for b in range(pb.batch_size)]
+    qo = np.concatenate([[0], np.cumsum(eb.extend)])
+    torch.set_num_threads(max(1, torch.get_num_threads()))
+    ref = O.forward_prefill_torch(q.cpu(), kv.k[0].cpu(), kv.v[0].cpu(), qo, idx, D ** -0.5)
+    err = float((out.double() - ref).abs().max())
+    assert err <= TOL["bfloat16"], err
 
 
 def test_extend_single_request_long_prefix_bf16():

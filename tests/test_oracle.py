@@ -129,7 +129,7 @@ def test_rope_partial_rotary_passes_tail_through():
 
 
 def test_prefill_no_prefix_uses_fresh_kv_and_prefix_uses_pool():
-    """attention/base.py:127-133: both branches must agree when the pool holds the fresh rows."""
+    """attention/base.py:90-96: both branches must agree when the pool holds the fresh rows."""
     rng = np.random.default_rng(7)
     Hq, Hkv, D, N = 4, 2, 32, 256
     k_pool = rng.standard_normal((N, Hkv, D))
@@ -156,3 +156,25 @@ def test_prefill_no_prefix_uses_fresh_kv_and_prefix_uses_pool():
     np.testing.assert_allclose(o1[0], ref_first[0, :, 0], atol=1e-12)
     ref0 = O.sdpa(q[3][None, :, None, :], kk[:, :, 90:94], vv[:, :, 90:94], D ** -0.5)
     np.testing.assert_allclose(o0[3], ref0[0, :, 0], atol=1e-12)
+
+
+def test_torch_prefill_restatement_matches_numpy_oracle():
+    """forward_prefill_torch (BLAS, for benchmark-sized parity tests) computes what
+    forward_prefill computes: ragged requests, with and without prefix, Lq = 1 unmasked."""
+    import torch
+
+    rng = np.random.default_rng(11)
+    prefix = np.array([0, 5, 33, 100, 0])
+    ext = np.array([1, 17, 64, 3, 9])
+    lens = prefix + ext
+    N, Hq, Hkv, D = 1024, 16, 8, 64
+    k, v = rng.standard_normal((N, Hkv, D)), rng.standard_normal((N, Hkv, D))
+    q = rng.standard_normal((int(ext.sum()), Hq, D))
+    table = np.stack([rng.permutation(N)[: lens.max()] for _ in lens]).astype(np.int32)
+    meta = O.prepare_prefill(table, np.arange(len(lens)), prefix, lens)
+    idx = [table[r, :n] for r, n in enumerate(lens)]
+    meta.kv_indices = idx
+    a = O.forward_prefill(q, None, None, k, v, meta, D ** -0.5)
+    b = O.forward_prefill_torch(torch.from_numpy(q), torch.from_numpy(k), torch.from_numpy(v), meta.q_offsets, idx,
+                                D ** -0.5).numpy()
+    assert np.abs(a - b).max() < 1e-12

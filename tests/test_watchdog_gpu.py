@@ -126,3 +126,56 @@ def test_extend_bad_page_is_reported_not_read(P):
     torch.cuda.synchronize()
     assert _device_error() == 0
     assert np.isfinite(to_np(out)).all()
+
+
+BAD_PLAN = 35  # kWdBadPlan
+
+
+@pytest.mark.parametrize("field", ["slot", "request"])
+def test_decode_bad_plan_segment_is_skipped_and_reported(field):
+    """A plan whose segment names a partial slot past the workspace, or a request past B,
+    is never followed: the segment is skipped (no partial row or output row is written
+    through it) and code 35 is reported. The workspace is then zeroed again (a skipped
+    segment leaves its request's merge counter short) and a correct plan is exact."""
+    import torch
+
+    from minisgl_b200 import _native as nat
+    from minisgl_b200.attention.base import paged_kv_indices
+
+    assert _device_error() == 0
+    rng = np.random.default_rng(5)
+    lens = rng.integers(200, 3000, size=9)
+    pb = W.allocate_pages(lens, 65536, 16, rng)
+    be, kv, hk, hv, rng = _backend(pb)
+    ind, idx, lpl = paged_kv_indices(pb.page_table, pb.rows, pb.lens, 16)
+    nc = 64
+    cta, segs, merge, n_part = nat.decode_plan(ind, lpl, 16, nc)
+    split = np.nonzero(segs[:, 3] >= 0)[0]
+    assert split.size >= 2
+    bad = segs.copy()
+    if field == "slot":
+        bad[split[0], 3] = n_part + 5
+    else:
+        bad[split[0], 0] = len(lens) + 3
+    q = rand(rng, (len(lens), 16, 128), "bfloat16")
+    qd = to_dev(q, "bfloat16")
+    ws_bytes = nat.decode_workspace_bytes(n_part, 16, 128)
+    ws = torch.zeros(ws_bytes, dtype=torch.uint8, device="cuda")
+    out = torch.zeros_like(qd)
+    stream = torch.cuda.current_stream().cuda_stream
+
+    def call(plan):
+        dev = [torch.from_numpy(np.ascontiguousarray(a)).cuda() for a in (idx, cta, plan, merge)]
+        nat.call("b2a_decode", qd.data_ptr(), kv.k[0].data_ptr(), kv.v[0].data_ptr(), pb.num_slots,
+                 dev[0].data_ptr(), 16, dev[1].data_ptr(), dev[2].data_ptr(), nc, dev[3].data_ptr(), n_part,
+                 len(lens), 16, 8, 128, float(128 ** -0.5), ws.data_ptr(), ws_bytes, out.data_ptr(),
+                 nat.B2A_DTYPE_BF16, stream)
+        torch.cuda.synchronize()
+
+    call(bad)
+    assert _device_error() == BAD_PLAN
+    ws.zero_()
+    call(segs)
+    assert _device_error() == 0
+    gidx, mask = O.naive_prepare_decode(pb.page_table, pb.rows, pb.lens)
+    assert max_abs(to_np(out), O.naive_forward_decode(q, hk, hv, gidx, mask, 128 ** -0.5)) <= TOL["bfloat16"]
