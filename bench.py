@@ -63,6 +63,7 @@ def parse_args():
     ap.add_argument("--no-extend", action="store_true", help="skip the config-3 extend measurement")
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 long-context decode measurement")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 end-to-end offline measurement")
+    ap.add_argument("--no-page1", action="store_true", help="skip the page-size-1 decode measurement")
     return ap.parse_args()
 
 
@@ -239,7 +240,8 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
            "rank0": {"requests": int(len(lens)), "sum_ctx_tokens": int(lens.sum()), "bytes_per_call": nbytes,
                      "ms_per_call": round(ms, 4), "achieved": round(gbs, 1), "frac": round(gbs / peak, 4),
                      "n_partials": meta.n_partials, "pool_gb": round(need / 1e9, 1)},
-           "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+           "roofline": {"bound": "hbm", "kernel": "decode_mma_kernel<4> (mma.sync tensor cores, TMA boxes)",
+                        "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
                         "frac": round(gbs / peak, 4), "peak_kind": kind},
            "clocks_rank0": clk,
            "config": {"workload": "config5: Qwen3-8B attention (32q/8kv/128), bf16, page 16, 1024 seqs, "
@@ -250,7 +252,74 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
     return out
 
 
-def measure_e2e_offline(dev, rank: int, world: int, seed: int):
+def measure_decode_page1(dev, seed: int, steps: int, warmup: int):
+    """Config-2 decode shapes at the reference's default page size 1 (engine/config.py:12).
+
+    One layer's pool (262144 slots, 16q/8kv/128, bf16), B = 128 requests with L ~ U[100, 2048]
+    from the config-2 generator. Two slot layouts: a seeded random permutation of the pool
+    (every token on its own slot, the worst case), and allocator order (a fresh
+    page-size-1 free list hands each prompt one run of consecutive slots,
+    scheduler/cache.py:28-72). Each call streams ~560 MB > L2.
+    """
+    import torch
+
+    from minisgl_b200 import MHAKVCache
+    from minisgl_b200 import workloads as W
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.config import qwen3_0_6b
+
+    cfg = qwen3_0_6b()
+    Hq, Hkv, D = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim
+    c = W.CONFIG2
+    N = c["num_slots"]
+    lens = W.config2_batch(seed=seed).lens
+    kv = MHAKVCache(1, N, Hkv, D, torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(seed)
+    kv.k[0].normal_(generator=gen)
+    kv.v[0].normal_(generator=gen)
+    q = torch.randn((len(lens), Hq, D), device=dev, generator=gen).to(torch.bfloat16)
+    peak, kind = measured_peaks()
+    nbytes = decode_bytes(lens, 1, Hq, Hkv, D, 2)
+    out = {"metric": "decode-attn HBM GB/s at page size 1 (one layer call)", "unit": "GB/s",
+           "bytes_per_call": nbytes, "config": {"workload": "config2 shapes at page size 1: B=128, L~U[100,2048], "
+                                                             "16q/8kv/128, bf16, 262144-slot pool", "sum_ctx_tokens": int(lens.sum())}}
+    rng = np.random.default_rng(seed + 5)
+    layouts = {"random_slots": W.permutation_slots(lens, N, rng),
+               "allocator_order": W.allocate_pages(lens, N, 1, rng)}
+    # allocator order: consecutive runs in request order (a fresh free list), not shuffled
+    alloc = layouts["allocator_order"]
+    off = 0
+    for b, L in enumerate(lens.tolist()):
+        alloc.page_table[b, :L] = np.arange(off, off + L, dtype=np.int32)
+        off += L
+    for name, pb in layouts.items():
+        be = B200AttnBackend(cfg, kv, pb.page_table, page_size=1)
+        meta = be.decode_metadata_from_lens(pb.rows, pb.lens)
+        for _ in range(max(warmup, 3)):
+            be.forward_decode(q, 0, meta)
+        torch.cuda.synchronize()
+        evs = []
+        for _ in range(max(steps, 20)):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            be.forward_decode(q, 0, meta)
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
+        ms = float(np.mean([a.elapsed_time(b) for a, b in evs]))
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        out[name] = {"value": round(gbs, 1), "ms_per_call": round(ms, 4),
+                     "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": peak, "unit": "GB/s",
+                                  "frac": round(gbs / peak, 4), "peak_kind": kind},
+                     "kernel": "decode_kernel (1-D bulk copies of slot runs)"}
+        del be, meta
+    out["value"] = out["random_slots"]["value"]
+    del kv, q
+    torch.cuda.empty_cache()
+    return out
+
+
+def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = False):
     """Config 4: end-to-end offline generation through the engine harness (output tok/s).
 
     Random-init Qwen3-0.6B (bf16), 256 prompts of U[100,1024] random token ids,
@@ -273,8 +342,13 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int):
 
     from minisgl_b200.engine.router import route_requests
 
-    c = W.CONFIG4
-    prompts_all, outs_all = W.config4_workload(seed=seed)
+    if shared:
+        # 16 system prompts of U[512, 2048] tokens, each starting 16 requests
+        c = W.CONFIG4_SHARED
+        prompts_all, outs_all, _ = W.config4_shared_workload(seed=seed)
+    else:
+        c = W.CONFIG4
+        prompts_all, outs_all = W.config4_workload(seed=seed)
     cost = np.array([len(p) for p in prompts_all]) + outs_all
     mine = route_requests(prompts_all, cost, world, page_size=c["page_size"])[rank]
     prompts = [prompts_all[i] for i in mine]
@@ -298,26 +372,38 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int):
         assert [len(r["token_ids"]) for r in res] == outs
         llm.cache.check_integrity()
         stats = torch.tensor([elapsed], dtype=torch.float64, device=dev)
-        tot = torch.tensor([float(sum(outs))], dtype=torch.float64, device=dev)
+        tot = torch.tensor([float(sum(outs)), float(llm.num_prefix_hit_tokens), float(llm.num_prefill_tokens)],
+                           dtype=torch.float64, device=dev)
+        hits_per_rank = torch.zeros(world, dtype=torch.float64, device=dev)
+        hits_per_rank[rank] = float(llm.num_prefix_hit_tokens)
         if world > 1:
             dist.all_reduce(stats, op=dist.ReduceOp.MAX)
             dist.all_reduce(tot, op=dist.ReduceOp.SUM)
-        tps = tot.item() / stats.item()
-        out = {"metric": "end-to-end output tok/s (offline, config 4)", "value": round(tps, 1),
+            dist.all_reduce(hits_per_rank, op=dist.ReduceOp.SUM)
+        tps = tot[0].item() / stats.item()
+        name = "config 4, shared prefixes" if shared else "config 4"
+        out = {"metric": f"end-to-end output tok/s (offline, {name})", "value": round(tps, 1),
                "unit": "tok/s", "higher_is_better": True, "scaling": "strong (256 requests split across ranks)",
                # the reference's published figure for this workload shape (README.md:84, Apple M5 Ultra,
                # Metal attention + overlap, real weights, temperature 0.6)
                "vs_published": {"value": 4427.0, "hardware": "Apple M5 Ultra (Metal)", "ratio": round(tps / 4427.0, 2)},
                "wall_s_max_rank": round(stats.item(), 3),
+               "prefix_hit_tokens_all": int(tot[1].item()), "prefill_tokens_all": int(tot[2].item()),
+               "prefix_hit_tokens_per_rank": [int(x) for x in hits_per_rank.tolist()],
                "rank0": {"requests": len(outs), "output_tokens": int(sum(outs)), "wall_s": round(elapsed, 3),
                          "prefill_tokens": llm.num_prefill_tokens, "prefix_hit_tokens": llm.num_prefix_hit_tokens,
                          "prefill_steps": llm.num_steps["prefill"], "decode_steps": llm.num_steps["decode"],
                          "time_s": {k: round(v, 3) for k, v in llm.timing.items()},
                          "kv_pool_gb": round(llm.engine.kv_cache.nbytes / 1e9, 2),
                          "model_gb": round(llm.engine.model.nbytes / 1e9, 2)},
-               "config": {"workload": "config4: random-init Qwen3-0.6B bf16, 256 reqs, input/output U[100,1024], "
-                                      "random ids, concurrency 128, greedy, ignore_eos, radix on, overlap on, "
-                                      "chunked prefill 4096, page 16, 131072 KV tokens",
+               "config": {"workload": ("config4 with shared prefixes: 16 system prompts U[512,2048] x 16 requests, "
+                                       "user part U[100,1024], outputs U[100,1024]; random-init Qwen3-0.6B bf16, "
+                                       "concurrency 128, greedy, ignore_eos, radix on, overlap on, chunked prefill 4096, "
+                                       "page 16, 262144 KV tokens; routed by first-page prefix affinity")
+                           if shared else
+                           "config4: random-init Qwen3-0.6B bf16, 256 reqs, input/output U[100,1024], "
+                           "random ids, concurrency 128, greedy, ignore_eos, radix on, overlap on, "
+                           "chunked prefill 4096, page 16, 131072 KV tokens",
                           "input_tokens_all": int(sum(len(p) for p in prompts_all)),
                           "output_tokens_all": int(outs_all.sum())},
                "data": "synthetic (random token ids, random weights)"}
@@ -353,8 +439,13 @@ def extend_executed_flops(prefix: np.ndarray, extend: np.ndarray, Hq: int, Hkv: 
     return float(blocks) * Hkv * 2 * (2 * 128 * KB * D)
 
 
-def measure_extend(dev, seed: int, steps: int, warmup: int):
-    """Config 3: 32 ragged requests with a cached radix prefix, fused RoPE+store then extend attention."""
+def measure_extend(dev, seed: int, steps: int, warmup: int, page_size: int | None = None):
+    """Config 3: 32 ragged requests with a cached radix prefix, fused RoPE+store then extend attention.
+
+    page_size None is config 3's page size 16 (the tcgen05 kernel reads the pool directly);
+    page_size 1 is the reference's default: the backend packs each request's KV rows into
+    16-slot pages (b2a_pack_kv) and runs the same kernel on them, both inside the timed call.
+    """
     import torch
 
     from minisgl_b200 import MHAKVCache
@@ -365,7 +456,7 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
 
     cfg = qwen3_0_6b()
     Hq, Hkv, D = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim
-    eb = W.config3_batch(seed=seed)
+    eb = W.config3_batch(seed=seed, page_size=page_size)
     pb = eb.paged
     kv = MHAKVCache(1, pb.num_slots, Hkv, D, torch.bfloat16, device=dev)
     gen = torch.Generator(device=dev).manual_seed(seed)
@@ -417,7 +508,7 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
     tf = flops / (ms * 1e-3) / 1e12
     from minisgl_b200 import _native as nat
 
-    tile = nat.extend_tile_q(Hq, Hkv, D, nat.B2A_DTYPE_BF16, pb.page_size)
+    tile = nat.extend_tile_q(Hq, Hkv, D, nat.B2A_DTYPE_BF16, max(pb.page_size, 16))
     tc = tile == 2 * (128 // (Hq // Hkv))
     # tile-padded work the tensor cores run (partial query tiles, masked key blocks)
     exe = extend_executed_flops(eb.prefix, eb.extend, Hq, Hkv, D) if tc else None
@@ -430,7 +521,8 @@ def measure_extend(dev, seed: int, steps: int, warmup: int):
             "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(tf / peak, 4), "peak_kind": kind + " (bf16 dense, burst)"},
             "config": {"workload": "config3: 32 ragged requests, prefix U[0,4096] page-aligned (+1 unaligned), "
-                                   "extend U[64,512], 16q/8kv/128, bf16, page 16, RoPE theta 1e6 fused store",
+                                   f"extend U[64,512], 16q/8kv/128, bf16, page {pb.page_size}, RoPE theta 1e6 fused store"
+                                   + (" (KV rows packed into 16-slot pages inside the timed call)" if pb.page_size < 16 else ""),
                        "tokens": T, "sum_prefix": int(eb.prefix.sum()), "tile_q_tokens": tile,
                        "kernel": "extend_tc2_kernel (tcgen05, 2 x 128-row tiles)" if tile == 2 * (128 // (Hq // Hkv)) else "extend_simt_kernel"},
             # config 3': the fused RoPE + KV store of the same T tokens (HBM-bound)
@@ -479,7 +571,8 @@ def config2_config(W, world: int, B: int, sum_ctx: int, layers: int) -> dict:
 
 
 DECODE_PROFILE = ROOT / "profiles" / "decode_kernel_config2.md"
-DECODE_SOURCES = ("mini-sglang-mlx_b200/csrc/decode.cuh", "mini-sglang-mlx_b200/csrc/common.cuh")
+DECODE_SOURCES = ("mini-sglang-mlx_b200/csrc/decode.cuh", "mini-sglang-mlx_b200/csrc/decode_mma.cuh",
+                  "mini-sglang-mlx_b200/csrc/common.cuh")
 
 
 def decode_sources_digest() -> str:
@@ -509,7 +602,7 @@ def decode_traffic():
         return None, "ncu summary has no traffic line"
     if m.group(2) != decode_sources_digest():
         return None, f"stale: captured on decode sources {m.group(2)}, timed on {decode_sources_digest()}"
-    return int(m.group(1)), f"ncu capture of decode_kernel on config-2 layer 0, seed 0, decode sources {m.group(2)}"
+    return int(m.group(1)), f"ncu capture of the decode launch on config-2 layer 0, seed 0, decode sources {m.group(2)}"
 
 
 # ------------------------------------------------------------------ reference arm
@@ -746,8 +839,11 @@ def run_ours(args):
     torch.cuda.synchronize()
     torch.cuda.empty_cache()
     ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
+    ext1 = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup, page_size=1)
+    dec1 = None if args.no_page1 else measure_decode_page1(dev, args.seed + 31 * rank, args.steps, args.warmup)
     c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps)
     e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed)
+    e2e4s = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, shared=True)
 
     line = None
     if rank == 0:
@@ -783,10 +879,16 @@ def run_ours(args):
             line["cpu_baseline"] = cpu
         if ext is not None:
             line["extend_config3"] = ext
+        if ext1 is not None:
+            line["extend_config3_p1"] = ext1
+        if dec1 is not None:
+            line["decode_config2_p1"] = dec1
         if c5 is not None:
             line["decode_config5"] = c5
         if e2e4 is not None:
             line["e2e_offline_config4"] = e2e4
+        if e2e4s is not None:
+            line["e2e_offline_config4_shared"] = e2e4s
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()

@@ -291,6 +291,21 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
 int b2a_swiglu(const void* gate_up, int64_t row_stride, void* out, int64_t rows, int F, int dtype,
                void* stream);
 
+/* ------------------------------------------------------------------------
+ * RMSNorm of hidden rows with an optional row gather (engine harness).
+ * Replaces nn.RMSNorm (python/minisgl_mlx/models/transformer.py:77-82, the
+ * two norms of every decoder layer) and, with `rows`, the last-token gather
+ * plus final norm of CausalLM.__call__ (:109-113) in one launch:
+ *   y[i] = x[r] / sqrt(mean(x[r]^2) + eps) * w,  r = rows ? rows[i] : i,
+ * in fp32, rounded once to `dtype`. x: x_rows rows of H elements, row i at
+ * x + i * x_row_stride; y: contiguous [n_rows, H]; w: [H]. All 16-byte
+ * aligned; H a multiple of 32 * (16 / element size), at most 16 vectors per
+ * lane. A gather index outside [0, x_rows) skips that row and records device
+ * error 32.
+ * ------------------------------------------------------------------------ */
+int b2a_rmsnorm(const void* x, int64_t x_row_stride, int64_t x_rows, const int32_t* rows, int64_t n_rows,
+                const void* w, float eps, int H, void* y, int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -15,10 +15,12 @@
 #include "b200attn.h"
 #include "common.cuh"
 #include "decode.cuh"
+#include "decode_mma.cuh"
 #include "extend_simt.cuh"
 #include "extend_tc.cuh"
 #include "pack_kv.cuh"
 #include "metadata.cuh"
+#include "rmsnorm.cuh"
 #include "rope_store.cuh"
 #include "swiglu.cuh"
 
@@ -552,6 +554,35 @@ static int decode_common(const void* q, const void* k_pool, const void* v_pool, 
   a.stage_bytes = c.stage_bytes;
   cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
   const int G = Hq / Hkv;
+  if (cta_indptr != nullptr && b2a::decode_mma_supported(Hq, Hkv, D, dtype, plog)) {
+    // tensor-core decode: TMA boxes {64 features, 1 head, 16 tokens} per page run
+    if (num_slots > 0x7fffffffLL - 64) return fail(B2A_ERR_INVALID, "decode: num_slots must be < 2^31");
+    auto enc = b2a::tensor_map_encoder(g_err);
+    if (!enc) return fail(B2A_ERR_CUDA, "decode: %s", g_err.c_str());
+    CUtensorMap km, vm;
+    const uint64_t row = (uint64_t)D * 2;
+    if (!b2a::encode_3d(enc, &km, k_pool, (uint64_t)D, (uint64_t)Hkv, (uint64_t)num_slots, row, row * Hkv, 64, 1,
+                        b2a::kMmaTok) ||
+        !b2a::encode_3d(enc, &vm, v_pool, (uint64_t)D, (uint64_t)Hkv, (uint64_t)num_slots, row, row * Hkv, 64, 1,
+                        b2a::kMmaTok))
+      return fail(B2A_ERR_INVALID, "decode: cuTensorMapEncodeTiled rejected the pool tensor map");
+    a.NCW = Hkv;
+    a.WPH = 1;
+    a.NSTAGE = b2a::decode_mma_nstage(Hkv, kSmemLimit);
+    a.TS = b2a::kMmaTok;
+    const size_t smem = b2a::decode_mma_smem_layout(a.NSTAGE, Hkv).total + 1024;
+    auto launch = [&](auto kern) -> int {
+      if (int rc = ensure_smem((const void*)kern, smem, "decode_mma")) return rc;
+      launch_pdl(kern, dim3(grid), dim3((Hkv + 1) * 32), smem, st, km, vm, a);
+      return check_launch("decode_mma_kernel");
+    };
+    switch (G) {
+      case 4:
+        return launch(b2a::decode_mma_kernel<4>);
+      default:
+        return launch(b2a::decode_mma_kernel<8>);
+    }
+  }
   int rc = with_dtype<false>(dtype, [&](auto tag) {
     using Tt = decltype(tag);
     return with_d(D, [&](auto dc) {
@@ -739,6 +770,60 @@ int b2a_swiglu(const void* gate_up, int64_t row_stride, void* out, int64_t rows,
     b2a::swiglu_kernel<T><<<blocks, 256, 0, st>>>(reinterpret_cast<const T*>(gate_up), row_stride,
                                                    reinterpret_cast<T*>(out), rows, F);
     return check_launch("swiglu_kernel");
+  });
+}
+
+int b2a_rmsnorm(const void* x, int64_t x_row_stride, int64_t x_rows, const int32_t* rows, int64_t n_rows,
+                const void* w, float eps, int H, void* y, int dtype, void* stream) {
+  if (n_rows < 0 || x_rows < 0) return fail(B2A_ERR_INVALID, "negative row count");
+  if (n_rows == 0) return ok();
+  if (!x || !w || !y) return fail(B2A_ERR_INVALID, "NULL pointer argument");
+  if (!rows && n_rows > x_rows) return fail(B2A_ERR_INVALID, "n_rows %lld > x_rows %lld without a gather",
+                                           (long long)n_rows, (long long)x_rows);
+  if (!(eps >= 0.f)) return fail(B2A_ERR_INVALID, "eps must be >= 0");
+  const size_t es = dtype_size(dtype);
+  if (es == 0) return fail(B2A_ERR_UNSUPPORTED, "dtype %d", dtype);
+  const int ev = (int)(16 / es);
+  if (H <= 0 || H % (32 * ev)) return fail(B2A_ERR_UNSUPPORTED, "H = %d must be a multiple of %d", H, 32 * ev);
+  const int vpl = H / (32 * ev);
+  if (x_row_stride < H || (x_row_stride * (int64_t)es) % 16)
+    return fail(B2A_ERR_INVALID, "x_row_stride %lld: >= H and 16-byte multiple rows needed", (long long)x_row_stride);
+  if (!aligned(x, 16) || !aligned(y, 16) || !aligned(w, 16)) return fail(B2A_ERR_INVALID, "x/y/w must be 16-byte aligned");
+  if ((n_rows + 7) / 8 > 0x7fffffff) return fail(B2A_ERR_INVALID, "too many rows");
+  b2a::RmsNormArgs a;
+  a.x = x;
+  a.x_stride = x_row_stride;
+  a.rows = rows;
+  a.x_rows = x_rows;
+  a.y = y;
+  a.w = w;
+  a.n_rows = n_rows;
+  a.H = H;
+  a.eps = eps;
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const dim3 grid((unsigned)((n_rows + 7) / 8));
+  return with_dtype<true>(dtype, [&](auto tag) -> int {
+    using T = decltype(tag);
+    switch (vpl) {
+      case 1:
+        launch_pdl(b2a::rmsnorm_kernel<T, 1>, grid, dim3(256), 0, st, a);
+        break;
+      case 2:
+        launch_pdl(b2a::rmsnorm_kernel<T, 2>, grid, dim3(256), 0, st, a);
+        break;
+      case 4:
+        launch_pdl(b2a::rmsnorm_kernel<T, 4>, grid, dim3(256), 0, st, a);
+        break;
+      case 8:
+        launch_pdl(b2a::rmsnorm_kernel<T, 8>, grid, dim3(256), 0, st, a);
+        break;
+      case 16:
+        launch_pdl(b2a::rmsnorm_kernel<T, 16>, grid, dim3(256), 0, st, a);
+        break;
+      default:
+        return fail(B2A_ERR_UNSUPPORTED, "H = %d: %d vectors per lane not compiled (1, 2, 4, 8, 16)", H, vpl);
+    }
+    return check_launch("rmsnorm_kernel");
   });
 }
 

@@ -103,6 +103,22 @@ __device__ __forceinline__ void decode_get_seg(const DecodeArgs& a, int idx, int
   }
 }
 
+// Visit order of a CTA's segments [seg0, seg1). The plan lists them in page
+// order, so a CTA's last segment is usually the head of a request whose tail the
+// next CTA streams first; visited last, its merge would fall at the very end of
+// every CTA. When the last segment writes a partial it is visited first instead
+// (then the others in page order), so both pieces of such a request finish early
+// and the CTA that merges it does so while other CTAs are still streaming.
+__device__ __forceinline__ int decode_seg_at(const DecodeArgs& a, int seg0, int seg1, bool last_first, int i) {
+  if (!last_first) return seg0 + i;
+  return i == 0 ? seg1 - 1 : seg0 + i - 1;
+}
+
+__device__ __forceinline__ bool decode_last_first(const DecodeArgs& a, int seg0, int seg1) {
+  if (a.cta_indptr == nullptr || seg1 - seg0 < 2) return false;
+  return reinterpret_cast<const int4*>(a.segs)[seg1 - 1].w >= 0;
+}
+
 // A segment is used only if its request id is in [0, B) and, when it writes a
 // partial, its slot lies in its request's merge range inside the workspace.
 // Producer and consumers decide identically, so a rejected segment is skipped
@@ -342,7 +358,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
     const size_t rowB = a.row_bytes;
     int ctr = 0;
     bool ok = true;
-    for (int si = seg0; si < seg1 && ok; ++si) {
+    const bool last_first = decode_last_first(a, seg0, seg1);
+    for (int i = 0; i < seg1 - seg0 && ok; ++i) {
+      const int si = decode_seg_at(a, seg0, seg1, last_first, i);
       int b, pbeg, ntok, slot;
       decode_get_seg(a, si, b, pbeg, ntok, slot);
       if (!decode_seg_ok(a, b, slot)) continue;  // the consumers skip it too (and report it)
@@ -444,7 +462,9 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
   volatile int* s_last = reinterpret_cast<volatile int*>(smem + L.last_flag);
   const T* qbase = reinterpret_cast<const T*>(a.q);
   int ctr = 0;
-  for (int si = seg0; si < seg1; ++si) {
+  const bool last_first = decode_last_first(a, seg0, seg1);
+  for (int i = 0; i < seg1 - seg0; ++i) {
+    const int si = decode_seg_at(a, seg0, seg1, last_first, i);
     int b, pbeg, ntok, slot;
     decode_get_seg(a, si, b, pbeg, ntok, slot);
     if (!decode_seg_ok(a, b, slot)) {

@@ -10,11 +10,11 @@ from .managers import CacheManager, ChunkedReq, DecodeManager, PendingReq, Prefi
 from .model import Qwen3Model, Qwen3Spec, qwen3_0_6b_spec, tiny_spec
 from .radix import NaivePrefixCache, PrefixHandle, RadixPrefixCache, create_prefix_cache
 from .router import prefix_key, route_requests
-from .scheduler import LLM, Engine, EngineConfig, Scheduler
+from .scheduler import LLM, Engine, EngineConfig, HostScheduler, Scheduler
 
 __all__ = [
     "CacheManager", "ChunkedReq", "DecodeManager", "Engine", "EngineConfig", "LLM", "NaivePrefixCache",
-    "PendingReq", "PrefillManager", "PrefixHandle", "Qwen3Model", "Qwen3Spec", "RadixPrefixCache",
+    "HostScheduler", "PendingReq", "PrefillManager", "PrefixHandle", "Qwen3Model", "Qwen3Spec", "RadixPrefixCache",
     "Scheduler", "TableManager", "create_prefix_cache", "prefix_key", "qwen3_0_6b_spec", "route_requests",
     "tiny_spec",
 ]

@@ -12,7 +12,9 @@ Inputs are packed ``[T]`` token ids. GEMMs are cuBLAS through ``F.linear``;
 the two residual adds of a layer are folded into the o_proj and down GEMMs
 (``torch.addmm`` with beta = 1: one rounding instead of two), and SwiGLU is
 one library kernel (``b2a_swiglu``), as the reference's mx.compile'd
-``swiglu`` is one kernel. Weights are drawn N(0, 0.02) from a seeded generator (there are no
+``swiglu`` is one kernel. The RMSNorms are ``b2a_rmsnorm``; in prefill the
+final norm gathers the last tokens itself (one kernel for the gather and the
+norm). Weights are drawn N(0, 0.02) from a seeded generator (there are no
 checkpoints on this machine), norms start at 1.
 """
 
@@ -41,6 +43,23 @@ def swiglu(gate_up: torch.Tensor) -> torch.Tensor:
     nat.call("b2a_swiglu", gate_up.data_ptr(), gate_up.stride(0), out.data_ptr(), T, F2 // 2,
              dtype_code(gate_up.dtype), torch.cuda.current_stream().cuda_stream)
     return out
+
+
+def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, rows: torch.Tensor | None = None) -> torch.Tensor:
+    """RMSNorm of the rows of ``x`` ``[T, H]`` (b2a_rmsnorm), optionally of ``x[rows]`` only.
+
+    Reference: nn.RMSNorm of python/minisgl_mlx/models/transformer.py:77-82; with ``rows``
+    the last-token gather plus final norm of :109-113 in one kernel.
+    """
+    T, H = x.shape
+    assert x.stride(1) == 1 and w.dtype == x.dtype
+    n = T if rows is None else rows.numel()
+    y = torch.empty((n, H), dtype=x.dtype, device=x.device)
+    if rows is not None:
+        assert rows.dtype == torch.int32 and rows.is_contiguous()
+    nat.call("b2a_rmsnorm", x.data_ptr(), x.stride(0), T, 0 if rows is None else rows.data_ptr(), n, w.data_ptr(),
+             float(eps), H, y.data_ptr(), dtype_code(x.dtype), torch.cuda.current_stream().cuda_stream)
+    return y
 
 
 @dataclass(frozen=True)
@@ -110,16 +129,15 @@ class Qwen3Model:
         h = F.embedding(input_ids, self.embed)
         T = h.shape[0]
         for L in self.layers:
-            x = F.rms_norm(h, (spec.hidden_size,), L.in_norm, eps)
+            x = rms_norm(h, L.in_norm, eps)
             qkv = F.linear(x, L.qkv)
             q = qkv[:, : Hq * D].view(T, Hq, D)
             k = qkv[:, Hq * D: (Hq + Hkv) * D].view(T, Hkv, D)
             v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
             # q/k RMSNorm fused into the RoPE + KV-store kernel
             h = torch.addmm(h, L.attn(q, k, v, L.q_norm, L.k_norm, eps), L.o.t())
-            x = F.rms_norm(h, (spec.hidden_size,), L.post_norm, eps)
+            x = rms_norm(h, L.post_norm, eps)
             h = torch.addmm(h, swiglu(F.linear(x, L.gate_up)), L.down.t())
-        if batch.is_prefill:
-            h = h[batch.attn_metadata.last_indices.long()]
-        h = F.rms_norm(h, (spec.hidden_size,), self.norm, eps)
+        # prefill: only each request's last token is normed and projected (one gather + norm kernel)
+        h = rms_norm(h, self.norm, eps, batch.attn_metadata.last_indices if batch.is_prefill else None)
         return F.linear(h, self.embed)

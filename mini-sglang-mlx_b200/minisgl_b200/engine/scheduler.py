@@ -109,25 +109,81 @@ class _Step:
     start: torch.cuda.Event
 
 
-class Scheduler:
-    def __init__(self, cfg: EngineConfig, device: torch.device | None = None) -> None:
+class HostScheduler:
+    """The host half of the scheduler (scheduler/scheduler.py:75-222 without the forward):
+    admission and chunked prefill, page allocation, prefix-cache bookkeeping and the
+    processing of sampled tokens. It does no device work, so the same code serves the
+    engine and a host-only run (e.g. counting prefix-cache hits of a request partition)."""
+
+    def __init__(self, cfg: EngineConfig, page_table: np.ndarray, num_pages: int,
+                 device: torch.device | None = None) -> None:
         self.cfg = cfg
-        self.engine = Engine(cfg, device)
-        dev = self.engine.device
         P = cfg.page_size
-        self.table = TableManager(cfg.max_running_req, self.engine.page_table, dev)
-        self.cache = CacheManager(self.engine.num_pages, P, self.engine.page_table, cfg.cache_type)
+        self.table = TableManager(cfg.max_running_req, page_table, device or torch.device("cpu"))
+        self.cache = CacheManager(num_pages, P, page_table, cfg.cache_type)
         self.decode = DecodeManager(P)
         self.prefill = PrefillManager(self.cache, self.table, self.decode)
         self.finished_reqs: set = set()
         self.eos_token_ids: set = set()
-        self._stager = PinnedStager(slots=4)
-        self._host_ring = [torch.empty(cfg.max_running_req, dtype=torch.int32, pin_memory=True) for _ in range(4)]
-        self._ring_next = 0
         self.num_output_tokens = 0
         self.num_prefill_tokens = 0
         self.num_prefix_hit_tokens = 0  # prompt tokens served from the prefix cache
         self.num_steps = {"prefill": 0, "decode": 0}
+
+    def next_batch(self) -> Batch | None:
+        """Prefill first, else one decode step of every running request; pages allocated."""
+        batch = self.prefill.schedule_next_batch(self.cfg.max_extend_tokens) or self.decode.schedule_next_batch()
+        if batch is None:
+            return None
+        self.cache.allocate_paged(batch.reqs)
+        self.num_steps[batch.phase] += 1
+        if batch.is_prefill:
+            self.num_prefill_tokens += sum(r.extend_len for r in batch.reqs)
+            # a request's first chunk starts exactly at its prefix-cache hit
+            self.num_prefix_hit_tokens += sum(r.cached_len for r in batch.reqs
+                                              if r.cached_len == r.cache_handle.cached_len)
+        return batch
+
+    def process_tokens(self, batch: Batch, tokens: Sequence[int]) -> None:
+        """Append each request's sampled token; finished requests release their row and pages
+        (their KV goes to the prefix cache), a prefilled prompt's KV joins the prefix cache."""
+        new_finished = set()
+        with self.cache.lazy_free_region():
+            for req, tok in zip(batch.reqs, tokens):
+                if isinstance(req, ChunkedReq) or req in self.finished_reqs:
+                    # a chunk has no meaningful token; a request that finished one step earlier
+                    # was already placed into this batch, its extra token is dropped
+                    continue
+                req.append_host(tok)
+                finished = len(req.input_ids) >= req.max_device_len
+                if not req.sampling_params.ignore_eos:
+                    finished |= tok in self.eos_token_ids
+                self.on_token(req, tok, finished)
+                self.num_output_tokens += 1
+                if finished:
+                    self.decode.remove_req(req)
+                    self.table.free(req.table_idx)
+                    self.cache.cache_req(req, finished=True)
+                    new_finished.add(req)
+                elif batch.is_prefill:
+                    self.cache.cache_req(req, finished=False)  # the prompt's KV joins the prefix cache
+        self.finished_reqs = new_finished
+
+    def on_token(self, req: Req, token: int, finished: bool) -> None:
+        """Called for every sampled token in order (the offline front end collects them)."""
+
+    @property
+    def idle(self) -> bool:
+        return not (self.prefill.runnable or self.decode.runnable)
+
+
+class Scheduler(HostScheduler):
+    def __init__(self, cfg: EngineConfig, device: torch.device | None = None) -> None:
+        self.engine = Engine(cfg, device)
+        super().__init__(cfg, self.engine.page_table, self.engine.num_pages, self.engine.device)
+        self._stager = PinnedStager(slots=4)
+        self._host_ring = [torch.empty(cfg.max_running_req, dtype=torch.int32, pin_memory=True) for _ in range(4)]
+        self._ring_next = 0
         # seconds: host scheduling + input/metadata preparation + launches, host result
         # processing, host blocked on the GPU; GPU time of each phase (events around each step)
         self.timing = {"host_launch": 0.0, "host_process": 0.0, "host_wait": 0.0, "gpu_prefill": 0.0,
@@ -140,19 +196,17 @@ class Scheduler:
 
     # ------------------------------------------------------------ one step
     def _schedule_next_batch(self) -> Batch | None:
-        batch = self.prefill.schedule_next_batch(self.cfg.max_extend_tokens) or self.decode.schedule_next_batch()
+        batch = self.next_batch()
         if batch is not None:
             self._prepare(batch)
         return batch
 
     def _prepare(self, batch: Batch) -> None:
         reqs = batch.reqs
-        self.cache.allocate_paged(reqs)
         positions, out_loc = batch_positions_out_loc(batch, self.engine.page_table)
         rows = np.array([r.table_idx for r in reqs], dtype=np.int32)
         if batch.is_decode and self.graphs is not None and self.graphs.bucket_for(batch.size) is not None:
             # replayed from a CUDA graph: inputs and metadata go into the bucket's buffers in _forward
-            self.num_steps["decode"] += 1
             batch.graph_inputs = (rows, np.array([r.device_len for r in reqs], dtype=np.int64), positions, out_loc)
             return
         arrays = [positions, out_loc, rows]
@@ -173,11 +227,6 @@ class Scheduler:
         dev = self._stager.upload(arrays, self.engine.device)
         if mirror:
             page_table_scatter(self.engine.page_table_dev, *dev[-3:])
-        self.num_steps[batch.phase] += 1
-        if batch.is_prefill:
-            self.num_prefill_tokens += len(positions)
-            # a request's first chunk starts exactly at its prefix-cache hit
-            self.num_prefix_hit_tokens += sum(r.cached_len for r in reqs if r.cached_len == r.cache_handle.cached_len)
         batch.positions, batch.out_loc = dev[0], dev[1]
         batch.rows = dev[2]
         batch.input_ids = dev[3] if batch.is_prefill else self.table.token_pool[dev[2].long()]
@@ -212,32 +261,8 @@ class Scheduler:
         t1 = time.perf_counter()
         self.timing["host_wait"] += t1 - t0
         self.timing["gpu_" + step.batch.phase] += step.start.elapsed_time(step.done) * 1e-3
-        tokens = step.host_tokens.tolist()
-        new_finished = set()
-        with self.cache.lazy_free_region():
-            for req, tok in zip(step.batch.reqs, tokens):
-                if isinstance(req, ChunkedReq) or req in self.finished_reqs:
-                    # a chunk has no meaningful token; a request that finished one step earlier
-                    # was already placed into this batch, its extra token is dropped
-                    continue
-                req.append_host(tok)
-                finished = len(req.input_ids) >= req.max_device_len
-                if not req.sampling_params.ignore_eos:
-                    finished |= tok in self.eos_token_ids
-                self.on_token(req, tok, finished)
-                self.num_output_tokens += 1
-                if finished:
-                    self.decode.remove_req(req)
-                    self.table.free(req.table_idx)
-                    self.cache.cache_req(req, finished=True)
-                    new_finished.add(req)
-                elif step.batch.is_prefill:
-                    self.cache.cache_req(req, finished=False)  # the prompt's KV joins the prefix cache
-        self.finished_reqs = new_finished
+        self.process_tokens(step.batch, step.host_tokens.tolist())
         self.timing["host_process"] += time.perf_counter() - t1
-
-    def on_token(self, req: Req, token: int, finished: bool) -> None:
-        """Called for every sampled token in order (the offline front end collects them)."""
 
     # ------------------------------------------------------------ loops
     def overlap_step(self, last: _Step | None) -> _Step | None:
@@ -254,11 +279,6 @@ class Scheduler:
         if batch is not None:
             self._process(self._forward(batch))
         return batch is not None
-
-    @property
-    def idle(self) -> bool:
-        return not (self.prefill.runnable or self.decode.runnable)
-
 
 class LLM(Scheduler):
     """Offline batch generation (reference llm.py): token-id prompts in, token ids out."""

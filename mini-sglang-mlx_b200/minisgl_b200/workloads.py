@@ -137,6 +137,30 @@ def config4_workload(seed: int = 0, num_seqs: int | None = None):
     return prompts, out_lens
 
 
+CONFIG4_SHARED = dict(num_groups=16, per_group=16, sys_lo=512, sys_hi=2048, user_lo=100, user_hi=1024,
+                      max_output=1024, vocab_hi=10000, max_running_req=128, max_extend_tokens=4096,
+                      num_tokens=262144, page_size=16)
+
+
+def config4_shared_workload(seed: int = 0):
+    """Config 4 with shared prefixes: 16 system prompts of U[512, 2048] random token ids,
+    each the start of 16 requests whose own part is U[100, 1024] tokens; outputs
+    U[100, 1024]; the 256 requests arrive in a seeded random order. This is the traffic
+    the prefix cache (kvcache/radix_cache.py) and the prefix-affinity router exist for.
+    Returns (prompts, out_lens, group id of each request)."""
+    c = CONFIG4_SHARED
+    rng = np.random.default_rng(seed)
+    systems = [rng.integers(0, c["vocab_hi"] + 1, int(rng.integers(c["sys_lo"], c["sys_hi"] + 1))).astype(np.int32)
+               for _ in range(c["num_groups"])]
+    n = c["num_groups"] * c["per_group"]
+    group = np.repeat(np.arange(c["num_groups"]), c["per_group"])[rng.permutation(n)]
+    prompts = [np.concatenate([systems[g], rng.integers(0, c["vocab_hi"] + 1,
+                                                        int(rng.integers(c["user_lo"], c["user_hi"] + 1)))]).astype(np.int32)
+               for g in group.tolist()]
+    out_lens = rng.integers(100, c["max_output"] + 1, n).astype(np.int64)
+    return prompts, out_lens, group
+
+
 def shard_requests(costs: np.ndarray, world: int) -> List[np.ndarray]:
     """Longest-processing-time assignment of requests to `world` ranks.
 

@@ -111,6 +111,24 @@ def test_paged_split_decode(hq, hkv, d, P, dtype):
         assert err <= TOL[dtype], (nc, err)
 
 
+@pytest.mark.parametrize("hq,hkv", [(32, 4), (64, 16), (64, 8), (32, 8)])
+@pytest.mark.parametrize("P", [16, 64])
+def test_tensor_core_decode_shapes(hq, hkv, P):
+    """The tensor-core decode (decode_mma_kernel, bf16, D = 128, G = 4 or 8, Hkv 4/8/16,
+    page size >= 16): every kernel instance and ring depth it has, ragged last pages, pages
+    of 64 slots (16-token stages starting inside a page), forced splits and merges."""
+    rng = np.random.default_rng(13)
+    lens = rng.integers(1, 2500, size=21)
+    lens[:7] = [1, 2, 15, 16, 17, 63, 65]
+    pb = W.allocate_pages(lens, 65536, P, rng)
+    for nc in (None, 9, 400):
+        out, ref, meta = _run_backend_decode(pb, hq, hkv, 128, "bfloat16", num_ctas=nc, seed=4)
+        err = max_abs(out, ref)
+        assert err <= TOL["bfloat16"], (nc, err)
+        if nc == 400:
+            assert meta.n_partials > 0
+
+
 def test_config2_shape_decode_bf16():
     """Config 2 shapes (B=128, 16/8/128, page 16, pool 262144, fragmented pages), one layer."""
     pb = W.config2_batch(seed=0)
