@@ -64,6 +64,8 @@ def parse_args():
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 long-context decode measurement")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 end-to-end offline measurement")
     ap.add_argument("--no-page1", action="store_true", help="skip the page-size-1 decode measurement")
+    ap.add_argument("--c5-requests", type=int, default=None,
+                    help="config 5 with only its first N requests (profiling captures; default all 1024)")
     return ap.parse_args()
 
 
@@ -171,7 +173,7 @@ def cpu_sample(lens, page_table, P, Hq, Hkv, D, num_slots, steps, warmup, seed):
     return gbs, per_call, torch.get_num_threads()
 
 
-def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
+def measure_config5(dev, rank: int, world: int, seed: int, steps: int, n_requests: int | None = None):
     """Config 5: request-partitioned long-context decode at Qwen3-8B attention shape.
 
     1024 sequences, context log-uniform in [1024, 131072] (sum ~27.4 M tokens),
@@ -193,6 +195,8 @@ def measure_config5(dev, rank: int, world: int, seed: int, steps: int):
     cfg = qwen3_8b()
     Hq, Hkv, D, P = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim, c["page_size"]
     lens_all = W.config5_lens(seed=seed)
+    if n_requests:
+        lens_all = lens_all[:n_requests]
     mine = W.shard_requests(lens_all, world)[rank]
     lens = lens_all[mine]
     rng = np.random.default_rng(seed + 7 * rank)
@@ -571,8 +575,9 @@ def config2_config(W, world: int, B: int, sum_ctx: int, layers: int) -> dict:
 
 
 DECODE_PROFILE = ROOT / "profiles" / "decode_kernel_config2.md"
-DECODE_SOURCES = ("mini-sglang-mlx_b200/csrc/decode.cuh", "mini-sglang-mlx_b200/csrc/decode_mma.cuh",
-                  "mini-sglang-mlx_b200/csrc/common.cuh")
+# the sources of the config-2 decode launch (decode_kernel); the tensor-core decode
+# (decode_mma.cuh) serves G >= 4 only and is not in the headline roofline
+DECODE_SOURCES = ("mini-sglang-mlx_b200/csrc/decode.cuh", "mini-sglang-mlx_b200/csrc/common.cuh")
 
 
 def decode_sources_digest() -> str:
@@ -841,7 +846,7 @@ def run_ours(args):
     ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
     ext1 = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup, page_size=1)
     dec1 = None if args.no_page1 else measure_decode_page1(dev, args.seed + 31 * rank, args.steps, args.warmup)
-    c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps)
+    c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps, args.c5_requests)
     e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed)
     e2e4s = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, shared=True)
 
