@@ -64,6 +64,9 @@ def parse_args():
     ap.add_argument("--no-config5", action="store_true", help="skip the config-5 long-context decode measurement")
     ap.add_argument("--no-config4", action="store_true", help="skip the config-4 end-to-end offline measurement")
     ap.add_argument("--no-page1", action="store_true", help="skip the page-size-1 decode measurement")
+    ap.add_argument("--c4-requests", type=int, default=None,
+                    help="config 4 with only its first N requests (one rank's share at N = 256/world)")
+    ap.add_argument("--no-config4-shared", action="store_true", help="skip the shared-prefix config-4 line")
     ap.add_argument("--c5-requests", type=int, default=None,
                     help="config 5 with only its first N requests (profiling captures; default all 1024)")
     return ap.parse_args()
@@ -323,7 +326,7 @@ def measure_decode_page1(dev, seed: int, steps: int, warmup: int):
     return out
 
 
-def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = False):
+def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = False, n_requests: int | None = None):
     """Config 4: end-to-end offline generation through the engine harness (output tok/s).
 
     Random-init Qwen3-0.6B (bf16), 256 prompts of U[100,1024] random token ids,
@@ -353,6 +356,8 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
     else:
         c = W.CONFIG4
         prompts_all, outs_all = W.config4_workload(seed=seed)
+    if n_requests:
+        prompts_all, outs_all = prompts_all[:n_requests], outs_all[:n_requests]
     cost = np.array([len(p) for p in prompts_all]) + outs_all
     mine = route_requests(prompts_all, cost, world, page_size=c["page_size"])[rank]
     prompts = [prompts_all[i] for i in mine]
@@ -397,6 +402,7 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
                "rank0": {"requests": len(outs), "output_tokens": int(sum(outs)), "wall_s": round(elapsed, 3),
                          "prefill_tokens": llm.num_prefill_tokens, "prefix_hit_tokens": llm.num_prefix_hit_tokens,
                          "prefill_steps": llm.num_steps["prefill"], "decode_steps": llm.num_steps["decode"],
+                         "gpu_ms_per_decode_step": round(1e3 * llm.timing["gpu_decode"] / max(1, llm.num_steps["decode"]), 4),
                          "time_s": {k: round(v, 3) for k, v in llm.timing.items()},
                          "kv_pool_gb": round(llm.engine.kv_cache.nbytes / 1e9, 2),
                          "model_gb": round(llm.engine.model.nbytes / 1e9, 2)},
@@ -847,8 +853,9 @@ def run_ours(args):
     ext1 = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup, page_size=1)
     dec1 = None if args.no_page1 else measure_decode_page1(dev, args.seed + 31 * rank, args.steps, args.warmup)
     c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps, args.c5_requests)
-    e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed)
-    e2e4s = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, shared=True)
+    e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, n_requests=args.c4_requests)
+    e2e4s = (None if args.no_config4 or args.no_config4_shared else
+             measure_e2e_offline(dev, rank, world, args.seed, shared=True, n_requests=args.c4_requests))
 
     line = None
     if rank == 0:

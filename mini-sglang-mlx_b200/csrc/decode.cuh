@@ -278,31 +278,59 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* 
 // other CTAs of the same launch: consumer warp w takes query heads w, w + NCW, ...
 // The rows are read through L2 (ld.global.cg): another SM wrote them, and this
 // SM's L1 may still hold lines of the same workspace from an earlier launch.
+// Up to four partials are fetched at once and folded into a running (M, l, acc)
+// (the same online rescaling as the kernel's softmax), so a merge costs one L2
+// round trip per four partials instead of a dependent load chain per partial.
 template <typename T, int D>
 __device__ __forceinline__ void decode_merge_request(const DecodeArgs& a, int b, int p0, int p1, int warp,
                                                      int lane) {
   constexpr int EPT = D / 32;
+  constexpr int U = 4;  // partials fetched together: one L2 round trip per U partials
   const int Hq = a.Hq;
   for (int qh = warp; qh < Hq; qh += a.NCW) {
-    float M = kNegInf;
-    for (int p = p0; p < p1; ++p) M = fmaxf(M, __ldcg(a.ws_ml + ((size_t)p * Hq + qh) * 2));
-    float Lsum = 0.f, acc[EPT];
+    float M = kNegInf, Lsum = 0.f, acc[EPT];
 #pragma unroll
     for (int e = 0; e < EPT; ++e) acc[e] = 0.f;
-    for (int p = p0; p < p1; ++p) {
-      const float m = __ldcg(a.ws_ml + ((size_t)p * Hq + qh) * 2);
-      const float l = __ldcg(a.ws_ml + ((size_t)p * Hq + qh) * 2 + 1);
-      const float w = (m == kNegInf) ? 0.f : exp2f(m - M);
-      Lsum += l * w;
-      const float* src = a.ws_acc + ((size_t)p * Hq + qh) * D + lane * EPT;
+    for (int base = p0; base < p1; base += U) {
+      float m[U], l[U], o[U][EPT];
 #pragma unroll
-      for (int e = 0; e < EPT; e += 4) {
-        const float4 o = __ldcg(reinterpret_cast<const float4*>(src + e));
-        acc[e + 0] = fmaf(w, o.x, acc[e + 0]);
-        acc[e + 1] = fmaf(w, o.y, acc[e + 1]);
-        acc[e + 2] = fmaf(w, o.z, acc[e + 2]);
-        acc[e + 3] = fmaf(w, o.w, acc[e + 3]);
+      for (int u = 0; u < U; ++u) {
+        const int p = base + u;
+        if (p < p1) {
+          const float2 ml = __ldcg(reinterpret_cast<const float2*>(a.ws_ml + ((size_t)p * Hq + qh) * 2));
+          m[u] = ml.x;
+          l[u] = ml.y;
+          const float* src = a.ws_acc + ((size_t)p * Hq + qh) * D + lane * EPT;
+#pragma unroll
+          for (int e = 0; e < EPT; e += 4) {
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(src + e));
+            o[u][e] = v.x;
+            o[u][e + 1] = v.y;
+            o[u][e + 2] = v.z;
+            o[u][e + 3] = v.w;
+          }
+        } else {
+          m[u] = kNegInf;
+          l[u] = 0.f;
+#pragma unroll
+          for (int e = 0; e < EPT; ++e) o[u][e] = 0.f;
+        }
       }
+      float Mn = M;
+#pragma unroll
+      for (int u = 0; u < U; ++u) Mn = fmaxf(Mn, m[u]);
+      const float keep = (M == kNegInf) ? 0.f : exp2f(M - Mn);
+      Lsum *= keep;
+#pragma unroll
+      for (int e = 0; e < EPT; ++e) acc[e] *= keep;
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const float w = (m[u] == kNegInf) ? 0.f : exp2f(m[u] - Mn);
+        Lsum += l[u] * w;
+#pragma unroll
+        for (int e = 0; e < EPT; ++e) acc[e] = fmaf(w, o[u][e], acc[e]);
+      }
+      M = Mn;
     }
     const float inv = Lsum > 0.f ? 1.f / Lsum : 0.f;
 #pragma unroll

@@ -394,8 +394,9 @@ __global__ void __launch_bounds__(17 * 32, 1)
 // round (0.93 against 0.78 of the HBM peak).
 inline bool decode_mma_supported(int Hq, int Hkv, int D, int dtype, int page_log2) {
   const int G = Hkv > 0 ? Hq / Hkv : 0;
-  return dtype == 1 /* bf16 */ && D == 128 && page_log2 >= 4 && (Hkv == 4 || Hkv == 8 || Hkv == 16) &&
-         (G == 4 || G == 8);
+  // Hkv 4 or 8: two stages of 16 tokens (64 KB each at Hkv 8) fit in shared memory; Hkv 16 would
+  // need 128 KB stages and stays on decode_kernel
+  return dtype == 1 /* bf16 */ && D == 128 && page_log2 >= 4 && (Hkv == 4 || Hkv == 8) && (G == 4 || G == 8);
 }
 
 // Ring depth: as many 16-token stages as fit (at most 6) next to the barriers

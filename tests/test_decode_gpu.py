@@ -111,12 +111,13 @@ def test_paged_split_decode(hq, hkv, d, P, dtype):
         assert err <= TOL[dtype], (nc, err)
 
 
-@pytest.mark.parametrize("hq,hkv", [(32, 4), (64, 16), (64, 8), (32, 8)])
+@pytest.mark.parametrize("hq,hkv", [(32, 4), (16, 4), (64, 8), (32, 8), (64, 16)])
 @pytest.mark.parametrize("P", [16, 64])
 def test_tensor_core_decode_shapes(hq, hkv, P):
-    """The tensor-core decode (decode_mma_kernel, bf16, D = 128, G = 4 or 8, Hkv 4/8/16,
+    """The tensor-core decode (decode_mma_kernel, bf16, D = 128, G = 4 or 8, Hkv 4 or 8,
     page size >= 16): every kernel instance and ring depth it has, ragged last pages, pages
-    of 64 slots (16-token stages starting inside a page), forced splits and merges."""
+    of 64 slots (16-token stages starting inside a page), forced splits and merges; Hkv 16
+    (64q/16kv) is served by decode_kernel and must agree the same way."""
     rng = np.random.default_rng(13)
     lens = rng.integers(1, 2500, size=21)
     lens[:7] = [1, 2, 15, 16, 17, 63, 65]

@@ -18,10 +18,13 @@ def _ref(x, w, eps, rows=None):
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16", "float16"])
-@pytest.mark.parametrize("T,H", [(1, 1024), (128, 1024), (37, 256), (300, 4096)])
+@pytest.mark.parametrize("T,H", [(1, 1024), (128, 1024), (37, 256), (300, 2048), (64, 4096)])
 @pytest.mark.parametrize("gather", [False, True])
 def test_rmsnorm_matches_fp32_reference(dtype, T, H, gather):
     import torch
+
+    if dtype == "float32" and H > 2048:
+        pytest.skip("fp32 rows hold at most 16 vectors of 4 per lane (H <= 2048)")
 
     from minisgl_b200.engine.model import rms_norm
 
@@ -60,3 +63,14 @@ def test_rmsnorm_strided_rows_and_bad_gather_index():
     assert code.value == 32
     ok = torch.tensor([0, 2])
     assert torch.allclose(y[ok].float(), _ref(x, w, 1e-6, rows[ok]), rtol=2 ** -7, atol=0)
+
+
+def test_rmsnorm_rejects_rows_wider_than_compiled():
+    import torch
+
+    from minisgl_b200 import _native as nat
+    from minisgl_b200.engine.model import rms_norm
+
+    x = torch.zeros((2, 4096), dtype=torch.float32, device="cuda")
+    with pytest.raises(nat.B200AttnError, match="not compiled"):
+        rms_norm(x, torch.ones(4096, device="cuda"), 1e-6)
