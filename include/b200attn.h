@@ -42,7 +42,7 @@
 extern "C" {
 #endif
 
-#define B2A_ABI_VERSION 2
+#define B2A_ABI_VERSION 1
 
 #define B2A_DTYPE_F32 0
 #define B2A_DTYPE_BF16 1
@@ -244,21 +244,15 @@ int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, in
  * attends keys j <= Lkv - Lq + i (bottom-right causal, mx.fast SDPA
  * mask="causal"; for Lq == 1 this is "no mask").
  * b2a_extend_plan (host only) tiles every request into query tiles of
- * b2a_extend_tile_q() rows and places every (tile, kv head) unit on one of
- * `num_ctas` CTAs, longest first onto the least loaded CTA:
- *   work (out) : int32 [work_capacity * 4] = {request, q_tile_begin,
- *                q_tile_rows, cta << 8 | kv head}, grouped by cta (ascending),
- *                each CTA's units in the order it runs them; n_work = tiles x Hkv
- * b2a_extend launches `num_ctas` persistent CTAs (b2a_extend_num_ctas: one per
- * SM); pass the same value to both calls.
+ * b2a_extend_tile_q() rows and orders them longest-first:
+ *   work (out) : int32 [work_capacity * 4] = {request, q_tile_begin, q_tile_rows, 0}
  * The kernel is chosen by (dtype, D, Hq/Hkv, page_size): bf16 with D == 128,
  * GQA group 1/2/4/8 and page_size a multiple of 16 runs on tcgen05 tensor
  * cores (TMEM accumulators, TMA-fed tiles, 128/G query tokens per tile);
  * every other supported shape runs a SIMT fp32-accumulating kernel (64/G
- * tokens per tile, one CTA per work row). `work` must come from b2a_extend_plan
- * with the tile size b2a_extend_tile_q returns for the same arguments; a larger
- * tile is clamped and flagged through the watchdog word, and a row naming a
- * request past B or a kv head past Hkv is skipped (device error 35).
+ * tokens per tile). `work` must come from b2a_extend_plan with the tile size
+ * b2a_extend_tile_q returns for the same arguments; a larger tile is clamped
+ * and flagged through the watchdog word.
  * ------------------------------------------------------------------------ */
 int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* tile_q);
 
@@ -276,15 +270,14 @@ int b2a_pack_kv(const void* k_pool, const void* v_pool, int64_t num_slots, const
                 const int32_t* kv_indices, int page_size, const int32_t* tok_indptr,
                 const int32_t* out_page_indptr, int B, int64_t total_tokens, int Hkv, int D, int dtype,
                 void* k_out, void* v_out, int64_t out_slots, void* stream);
-int b2a_extend_num_ctas(int* num_ctas);
 int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr,
-                    const int32_t* kv_last_page_len, int B, int page_size, int tile_q, int Hkv,
-                    int num_ctas, int32_t* work, int work_capacity, int* n_work);
+                    const int32_t* kv_last_page_len, int B, int page_size, int tile_q,
+                    int32_t* work, int work_capacity, int* n_work);
 int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
                const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
                const int32_t* kv_last_page_len, int page_size, const int32_t* work, int n_work,
-               int num_ctas, int T, int B, int Hq, int Hkv, int D, float scale, void* out,
-               int dtype, void* stream);
+               int T, int B, int Hq, int Hkv, int D, float scale, void* out, int dtype,
+               void* stream);
 
 /* ------------------------------------------------------------------------
  * SwiGLU activation of the engine harness's MLP.

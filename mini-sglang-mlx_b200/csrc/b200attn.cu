@@ -8,7 +8,6 @@
 #include <cstring>
 #include <map>
 #include <mutex>
-#include <queue>
 #include <string>
 #include <utility>
 #include <vector>
@@ -828,20 +827,10 @@ int b2a_rmsnorm(const void* x, int64_t x_row_stride, int64_t x_rows, const int32
   });
 }
 
-int b2a_extend_num_ctas(int* num_ctas) {
-  if (!num_ctas) return fail(B2A_ERR_INVALID, "num_ctas is NULL");
-  const int sms = num_sms();
-  if (sms <= 0) return fail(B2A_ERR_CUDA, "no CUDA device");
-  *num_ctas = sms;  // one persistent CTA per SM (the tensor-core kernel owns an SM's TMEM)
-  return ok();
-}
-
 int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,
-                    int page_size, int tile_q, int Hkv, int num_ctas, int32_t* work, int work_capacity, int* n_work) {
+                    int page_size, int tile_q, int32_t* work, int work_capacity, int* n_work) {
   if (!qo_indptr || !kv_indptr || !work || !n_work) return fail(B2A_ERR_INVALID, "NULL plan argument");
   if (B < 0 || tile_q <= 0) return fail(B2A_ERR_INVALID, "B must be >= 0, tile_q > 0");
-  if (Hkv < 1 || Hkv > 255) return fail(B2A_ERR_INVALID, "Hkv = %d out of [1, 255]", Hkv);
-  if (num_ctas < 1 || num_ctas > (1 << 22)) return fail(B2A_ERR_INVALID, "num_ctas = %d out of [1, 2^22]", num_ctas);
   if (ilog2_exact(page_size) < 0) return fail(B2A_ERR_INVALID, "page_size %d must be a power of two", page_size);
   struct Item {
     int r, tb, nq;
@@ -860,53 +849,27 @@ int b2a_extend_plan(const int32_t* qo_indptr, const int32_t* kv_indptr, const in
     const int64_t prefix = Lkv - Lq;
     for (int tb = 0; tb < Lq; tb += tile_q) {
       const int nq = std::min(tile_q, Lq - tb);
-      // cost in 128-key blocks of the item's last row, plus one for the unit's set-up
-      items.push_back({r, tb, nq, (prefix + tb + nq + 127) / 128 + 1});
+      items.push_back({r, tb, nq, (int64_t)nq * (prefix + tb + nq)});
     }
   }
-  const int64_t n_units = (int64_t)items.size() * Hkv;
-  if (n_units > work_capacity)
-    return fail(B2A_ERR_WORKSPACE, "work_capacity %d < %lld rows (items x kv heads)", work_capacity, (long long)n_units);
+  if ((int)items.size() > work_capacity) return fail(B2A_ERR_WORKSPACE, "work_capacity %d < %zu tiles", work_capacity, items.size());
   std::stable_sort(items.begin(), items.end(), [](const Item& x, const Item& y) { return x.cost > y.cost; });
-  // Longest processing time first: each (item, kv head) unit goes to the least
-  // loaded CTA (ties to the lowest CTA id); units of equal cost (an item's heads)
-  // land on different CTAs at about the same time.
-  using Load = std::pair<int64_t, int>;
-  std::priority_queue<Load, std::vector<Load>, std::greater<Load>> heap;
-  for (int c = 0; c < num_ctas; ++c) heap.push({0, c});
-  std::vector<int> unit_cta((size_t)n_units);
-  std::vector<int> per_cta((size_t)num_ctas + 1, 0);
   for (size_t i = 0; i < items.size(); ++i) {
-    for (int h = 0; h < Hkv; ++h) {
-      Load L = heap.top();
-      heap.pop();
-      unit_cta[i * Hkv + h] = L.second;
-      per_cta[L.second + 1]++;
-      heap.push({L.first + items[i].cost, L.second});
-    }
+    work[4 * i + 0] = items[i].r;
+    work[4 * i + 1] = items[i].tb;
+    work[4 * i + 2] = items[i].nq;
+    work[4 * i + 3] = 0;
   }
-  for (int c = 0; c < num_ctas; ++c) per_cta[c + 1] += per_cta[c];
-  for (size_t i = 0; i < items.size(); ++i) {
-    for (int h = 0; h < Hkv; ++h) {
-      const int c = unit_cta[i * Hkv + h];
-      const int row = per_cta[c]++;
-      work[4 * row + 0] = items[i].r;
-      work[4 * row + 1] = items[i].tb;
-      work[4 * row + 2] = items[i].nq;
-      work[4 * row + 3] = (c << 8) | h;
-    }
-  }
-  *n_work = (int)n_units;
+  *n_work = (int)items.size();
   return ok();
 }
 
 int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots, const int32_t* qo_indptr,
                const int32_t* kv_indptr, const int32_t* kv_indices, const int32_t* kv_last_page_len, int page_size,
-               const int32_t* work, int n_work, int num_ctas, int T, int B, int Hq, int Hkv, int D, float scale,
-               void* out, int dtype, void* stream) {
+               const int32_t* work, int n_work, int T, int B, int Hq, int Hkv, int D, float scale, void* out,
+               int dtype, void* stream) {
   if (n_work < 0 || B < 0 || T < 0) return fail(B2A_ERR_INVALID, "negative size");
   if (n_work == 0) return ok();
-  if (num_ctas < 1 || num_ctas > (1 << 22)) return fail(B2A_ERR_INVALID, "num_ctas = %d out of [1, 2^22]", num_ctas);
   if (int rc = check_heads(Hq, Hkv, D)) return rc;
   if (!q || !k_pool || !v_pool || !qo_indptr || !kv_indptr || !kv_indices || !work || !out)
     return fail(B2A_ERR_INVALID, "NULL pointer argument");
@@ -922,7 +885,7 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
   if (extend_uses_tc(Hq, Hkv, D, dtype, plog)) {
     if (int rc = ensure_smem((const void*)b2a::extend_tc2_kernel, b2a::Tc2Smem::ALLOC, "extend_tc")) return rc;
     return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
-                                 plog, work, n_work, num_ctas, T, B, Hq, Hkv, scale, out, st, g_err);
+                                 plog, work, n_work, T, Hq, Hkv, scale, out, st, g_err);
   }
   if (G > b2a::kSimtRows) return fail(B2A_ERR_UNSUPPORTED, "GQA group %d too large", G);
   b2a::ExtendArgs a;
@@ -949,7 +912,7 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
         auto kern = b2a::extend_simt_kernel<Tt, Dc, Gc>;
         const size_t smem = b2a::extend_simt_smem(Dc);
         if (int rc = ensure_smem((const void*)kern, smem, "extend")) return rc;
-        kern<<<dim3((unsigned)n_work), b2a::kSimtThreads, smem, st>>>(a);  // one CTA per (item, kv head) row
+        kern<<<dim3(n_work, Hkv), b2a::kSimtThreads, smem, st>>>(a);
         return check_launch("extend_simt_kernel");
       });
     });

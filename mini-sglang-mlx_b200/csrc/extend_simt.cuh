@@ -6,7 +6,7 @@
 // (bottom-right causal). This kernel is the exact-fp32 path (parity 1e-5) and
 // the fallback for shapes the tcgen05 kernel does not cover.
 //
-// CTA = one work row (work item, kv head h). Tile rows = TQ tokens x G query heads
+// CTA = (work item, kv head h). Tile rows = TQ tokens x G query heads
 // (row = token * G + g), so the G heads of a GQA group share one pass over
 // K/V. K/V blocks of 32 keys are gathered from the pool page by page and
 // widened to fp32 in shared memory (K rows padded to D+1 floats so the
@@ -24,7 +24,7 @@ struct ExtendArgs {
   const int32_t* kv_indptr;
   const int32_t* kv_indices;
   const int32_t* kv_last_page_len;
-  const int32_t* work;  // int4 {request, q tile begin, q tile rows, cta << 8 | kv head}
+  const int32_t* work;  // int4 {request, q tile begin, q tile rows, 0}
   void* out;
   int64_t num_slots;
   int page_log2;
@@ -57,8 +57,7 @@ __global__ void __launch_bounds__(kSimtThreads) extend_simt_kernel(const ExtendA
 
   const int4 w = reinterpret_cast<const int4*>(a.work)[blockIdx.x];
   const int r = w.x, tb = w.y;
-  const int h = w.w & 255;  // kv head of the row (rows are grouped by the tensor-core kernel's CTA bins)
-  if (h >= a.Hkv) return;  // a row naming a kv head past Hkv is skipped
+  const int h = blockIdx.y;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int nq = min(w.z, kSimtRows / G);
   if (w.z > nq && tid == 0) watchdog_set(kWdTileTooLarge);

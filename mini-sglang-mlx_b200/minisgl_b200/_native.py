@@ -82,14 +82,13 @@ SIGNATURES = {
         c_int,
         [_P, _P, c_int64, _P, _P, c_int, _P, _P, c_int, c_int64, c_int, c_int, c_int, _P, _P, c_int64, _P],
     ),
-    "b2a_extend_num_ctas": (c_int, [ctypes.POINTER(c_int)]),
     "b2a_extend_plan": (
         c_int,
-        [_P, _P, _P, c_int, c_int, c_int, c_int, c_int, _P, c_int, ctypes.POINTER(c_int)],
+        [_P, _P, _P, c_int, c_int, c_int, _P, c_int, ctypes.POINTER(c_int)],
     ),
     "b2a_extend": (
         c_int,
-        [_P, _P, _P, c_int64, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_int, c_int,
+        [_P, _P, _P, c_int64, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_int,
          c_float, _P, c_int, _P],
     ),
     "b2a_swiglu": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, _P]),
@@ -167,26 +166,18 @@ def extend_tile_q(Hq: int, Hkv: int, D: int, dtype_code: int, page_size: int) ->
     return t.value
 
 
-def extend_num_ctas() -> int:
-    """Persistent CTAs of the extend kernel on the current device (b2a_extend_num_ctas)."""
-    n = c_int(0)
-    call("b2a_extend_num_ctas", ctypes.byref(n))
-    return n.value
-
-
 def extend_plan(qo_indptr: np.ndarray, kv_indptr: np.ndarray, kv_last_page_len: np.ndarray | None,
-                page_size: int, tile_q: int, Hkv: int, num_ctas: int) -> np.ndarray:
-    """Host-side work list (b2a_extend_plan): int32 [n_work, 4] rows {request, q tile begin,
-    q tile rows, cta << 8 | kv head}, one per (tile, kv head), grouped by CTA."""
+                page_size: int, tile_q: int) -> np.ndarray:
+    """Host-side tile list (b2a_extend_plan): int32 [n_work, 4], longest tiles first."""
     qo = np.ascontiguousarray(qo_indptr, dtype=np.int32)
     kv = np.ascontiguousarray(kv_indptr, dtype=np.int32)
     lpl = None if kv_last_page_len is None else np.ascontiguousarray(kv_last_page_len, dtype=np.int32)
     B = qo.shape[0] - 1
     total_q = int(qo[-1]) if B > 0 else 0
-    cap = max(1, (B + total_q // max(tile_q, 1) + 1) * Hkv)
+    cap = max(1, B + total_q // max(tile_q, 1) + 1)
     work = np.zeros(cap * 4, np.int32)
     n = c_int(0)
-    call("b2a_extend_plan", np_ptr(qo), np_ptr(kv), np_ptr(lpl), B, page_size, tile_q, Hkv, num_ctas,
+    call("b2a_extend_plan", np_ptr(qo), np_ptr(kv), np_ptr(lpl), B, page_size, tile_q,
          np_ptr(work), cap, ctypes.byref(n))
     return work[: 4 * n.value].reshape(-1, 4)
 

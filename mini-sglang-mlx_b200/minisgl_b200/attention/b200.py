@@ -98,8 +98,6 @@ class B200AttnBackend(BaseAttnBackend):
         with torch.cuda.device(self.device):
             nat.call("b2a_decode_num_ctas", self.Hq, self.Hkv, self.D, self.dtype_code, nat.ctypes.byref(n))
         self.num_ctas = n.value
-        with torch.cuda.device(self.device):
-            self.extend_ctas = nat.extend_num_ctas()
 
     # ------------------------------------------------------------ helpers
     @property
@@ -244,7 +242,7 @@ class B200AttnBackend(BaseAttnBackend):
             if tile16 != tile_q:  # the tensor-core kernel takes this shape once pages are 16 slots
                 return self._packed_extend_metadata(qo_indptr, np.asarray(lens, dtype=np.int64), kv_indptr,
                                                     kv_indices, P, tile16)
-        work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, tile_q, self.Hkv, self.extend_ctas)
+        work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
         dev = self._stager.upload([last_indices, qo_indptr, kv_indptr, kv_indices, lpl, work], self.device)
         return B200PrefillMetadata(
@@ -268,7 +266,7 @@ class B200AttnBackend(BaseAttnBackend):
         total_pages = int(out_page_indptr[-1])
         kv_indices = np.arange(total_pages, dtype=np.int32)
         lpl = np.where(npages > 0, lens - (npages - 1) * Q, 0).astype(np.int32)
-        work = nat.extend_plan(qo_indptr, out_page_indptr, lpl, Q, tile_q, self.Hkv, self.extend_ctas)
+        work = nat.extend_plan(qo_indptr, out_page_indptr, lpl, Q, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
         if int(tok_indptr[-1]) >= 2 ** 31:
             raise ValueError("packed extend: more than 2^31 KV rows in one batch")
@@ -316,7 +314,7 @@ class B200AttnBackend(BaseAttnBackend):
         nat.call(
             "b2a_extend", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), num_slots, meta.qo_indptr.data_ptr(),
             meta.kv_indptr.data_ptr(), meta.kv_indices.data_ptr(), meta.kv_last_page_len.data_ptr(),
-            meta.page_size, meta.work.data_ptr(), meta.n_work, self.extend_ctas, T, B, self.Hq, self.Hkv, self.D,
+            meta.page_size, meta.work.data_ptr(), meta.n_work, T, B, self.Hq, self.Hkv, self.D,
             float(self.scale), out.data_ptr(), self.dtype_code, current_stream_ptr(self.device),
         )
         return out

@@ -110,32 +110,21 @@ def test_decode_plan_rejects_bad_input():
         nat.decode_plan(np.array([0, 2], np.int32), np.array([17], np.int32), 16, 4)
 
 
-def test_extend_plan_tiles_units_and_balance():
-    """b2a_extend_plan: every request's rows covered once per kv head, units grouped by CTA,
-    each CTA's units longest first, loads balanced (longest processing time first)."""
+def test_extend_plan_tiles_and_order():
     eb = W.config3_batch(seed=0)
     P = eb.paged.page_size
     ind, idx, lpl = paged_kv_indices(eb.paged.page_table, eb.paged.rows, eb.paged.lens, P)
     qo = np.concatenate([[0], np.cumsum(eb.extend)]).astype(np.int32)
-    Hkv, nc = 8, 148
-    work = nat.extend_plan(qo, ind, lpl, P, 64, Hkv, nc)
+    work = nat.extend_plan(qo, ind, lpl, P, 64)
     rows = {}
-    for r, tb, nq, w in work.tolist():
+    for r, tb, nq, _ in work.tolist():
         assert 0 < nq <= 64 and tb % 64 == 0
-        rows[(r, w & 255)] = rows.get((r, w & 255), 0) + nq
-    assert rows == {(r, h): int(e) for r, e in enumerate(eb.extend) for h in range(Hkv)}
-    cta = work[:, 3] >> 8
-    assert (np.diff(cta) >= 0).all() and cta.min() >= 0 and cta.max() < nc
-    cost = np.array([(int(eb.prefix[r]) + tb + nq + 127) // 128 + 1 for r, tb, nq, _ in work.tolist()])
-    load = np.bincount(cta, weights=cost, minlength=nc)
-    for c in range(nc):  # a CTA runs its units longest first
-        mine = cost[cta == c]
-        assert (np.diff(mine) <= 0).all()
-    assert load.max() <= load.mean() * 1.1 + cost.max()
+        rows[r] = rows.get(r, 0) + nq
+    assert rows == {r: int(e) for r, e in enumerate(eb.extend)}
+    cost = [nq * (int(eb.prefix[r]) + tb + nq) for r, tb, nq, _ in work.tolist()]
+    assert cost == sorted(cost, reverse=True)
     with pytest.raises(ValueError, match="kv length"):
-        nat.extend_plan(np.array([0, 40], np.int32), np.array([0, 1], np.int32), np.array([8], np.int32), 16, 64, 8, 4)
-    with pytest.raises(ValueError, match="Hkv"):
-        nat.extend_plan(qo, ind, lpl, P, 64, 0, nc)
+        nat.extend_plan(np.array([0, 40], np.int32), np.array([0, 1], np.int32), np.array([8], np.int32), 16, 64)
 
 
 def test_rope_tables():
