@@ -8,7 +8,9 @@ the stored k is bit-identical to the k the backend sees.
 
 Inverse frequencies (reference layers.py:31-43,59-74 and mx.fast.rope's
 definition inv_freq_i = base^(-2i/dims), or 1/freqs[i] for llama3) are
-computed once on the host in float64 and rounded to float32; the kernel uses
+computed once on the host: base^(-2i/dims) in float64 rounded to float32,
+the llama3 periods in float32 in the reference's own operation order (their
+reciprocal is one correctly rounded float32 division); the kernel uses
 angle = fl32(fl32(pos * scale) * inv_freq[i]) with an accurate sincos.
 """
 
@@ -27,14 +29,18 @@ from .kvcache.pool import current_stream_ptr, dtype_code
 
 
 def llama3_freqs(dims: int, base: float, scaling: Dict[str, Any]) -> np.ndarray:
-    """Wavelength-scaled rotary periods of Llama 3 (reference layers.py:59-74), float64."""
+    """Wavelength-scaled rotary periods of Llama 3 (reference layers.py:59-74), float32.
+
+    The reference evaluates this on MLX float32 arrays; the same operations in the same
+    order on numpy float32 arrays (Python scalars never widen them) give the same table.
+    """
     factor = scaling["factor"]
     low = scaling.get("low_freq_factor", 1.0)
     high = scaling.get("high_freq_factor", 4.0)
     old_ctx = scaling.get("original_max_position_embeddings", 8192)
     low_wavelen = old_ctx / low
     high_wavelen = old_ctx / high
-    freqs = base ** (np.arange(0, dims, 2, dtype=np.float64) / dims)
+    freqs = base ** (np.arange(0, dims, 2, dtype=np.float32) / dims)
     wavelens = 2 * math.pi * freqs
     freqs = np.where(wavelens > low_wavelen, freqs * factor, freqs)
     is_medium = (wavelens > high_wavelen) & (wavelens < low_wavelen)
