@@ -46,25 +46,32 @@ __global__ void __launch_bounds__(256) rmsnorm_kernel(const RmsNormArgs a) {
     }
   }
   const T* xr = reinterpret_cast<const T*>(a.x) + r * a.x_stride;
-  float v[VPL][EV];
-  float ss = 0.f;
+  const T* wr = reinterpret_cast<const T*>(a.w);
+  // rows of up to 8 vectors a lane load the weights together with the row (one memory
+  // round trip, not two); wider rows load them after the reduction (registers)
+  constexpr bool kPre = VPL <= 8;
+  constexpr int WV = kPre ? VPL : 1;
+  float v[VPL][EV], wv[WV][EV];
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
     load_vec<T, EV>(xr + (size_t)(k * 32 + lane) * EV, v[k]);
+    if constexpr (kPre) load_vec<T, EV>(wr + (size_t)(k * 32 + lane) * EV, wv[k]);
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < VPL; ++k)
 #pragma unroll
     for (int e = 0; e < EV; ++e) ss = fmaf(v[k][e], v[k][e], ss);
-  }
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
   const float inv = rsqrtf(ss / (float)a.H + a.eps);
   T* yr = reinterpret_cast<T*>(a.y) + i * (int64_t)a.H;
-  const T* wr = reinterpret_cast<const T*>(a.w);
 #pragma unroll
   for (int k = 0; k < VPL; ++k) {
-    float wv[EV];
-    load_vec<T, EV>(wr + (size_t)(k * 32 + lane) * EV, wv);
+    float* w = wv[kPre ? k : 0];
+    if constexpr (!kPre) load_vec<T, EV>(wr + (size_t)(k * 32 + lane) * EV, wv[0]);
 #pragma unroll
-    for (int e = 0; e < EV; ++e) v[k][e] = v[k][e] * inv * wv[e];
+    for (int e = 0; e < EV; ++e) v[k][e] = v[k][e] * inv * w[e];
     store_vec<T, EV>(yr + (size_t)(k * 32 + lane) * EV, v[k]);
   }
 }
