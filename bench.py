@@ -67,6 +67,8 @@ def parse_args():
     ap.add_argument("--c4-requests", type=int, default=None,
                     help="config 4 with only its first N requests (one rank's share at N = 256/world)")
     ap.add_argument("--no-config4-shared", action="store_true", help="skip the shared-prefix config-4 line")
+    ap.add_argument("--no-fused-proj", action="store_true",
+                    help="config 4 with the unfused projections (cuBLAS GEMMs + separate norm / SwiGLU kernels)")
     ap.add_argument("--c5-requests", type=int, default=None,
                     help="config 5 with only its first N requests (profiling captures; default all 1024)")
     return ap.parse_args()
@@ -326,7 +328,8 @@ def measure_decode_page1(dev, seed: int, steps: int, warmup: int):
     return out
 
 
-def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = False, n_requests: int | None = None):
+def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = False, n_requests: int | None = None,
+                        fused_proj: bool = True):
     """Config 4: end-to-end offline generation through the engine harness (output tok/s).
 
     Random-init Qwen3-0.6B (bf16), 256 prompts of U[100,1024] random token ids,
@@ -337,6 +340,8 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
     warm-up generation. Under torchrun the requests are partitioned by the
     prefix-affinity router (engine/router.py: first-page groups, placed
     longest-first) and the job throughput is all outputs / slowest rank.
+    Decode steps of <= 64 requests run the layers' projections as b2a_proj
+    launches (norm, residual adds and SwiGLU fused) unless ``fused_proj`` is off.
     """
     import time
 
@@ -363,7 +368,8 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
     prompts = [prompts_all[i] for i in mine]
     outs = [int(outs_all[i]) for i in mine]
     cfg = EngineConfig(spec=qwen3_0_6b_spec(), dtype="bfloat16", max_running_req=c["max_running_req"],
-                       page_size=c["page_size"], num_tokens=c["num_tokens"], max_extend_tokens=c["max_extend_tokens"])
+                       page_size=c["page_size"], num_tokens=c["num_tokens"], max_extend_tokens=c["max_extend_tokens"],
+                       fused_proj=fused_proj)
     with torch.cuda.device(dev):
         llm = LLM(cfg, device=dev)
         rng = np.random.default_rng(seed + 1)
@@ -404,6 +410,7 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
                          "prefill_steps": llm.num_steps["prefill"], "decode_steps": llm.num_steps["decode"],
                          "gpu_ms_per_decode_step": round(1e3 * llm.timing["gpu_decode"] / max(1, llm.num_steps["decode"]), 4),
                          "time_s": {k: round(v, 3) for k, v in llm.timing.items()},
+                         "fused_proj_steps_le_64": llm.engine.model.fused_proj,
                          "kv_pool_gb": round(llm.engine.kv_cache.nbytes / 1e9, 2),
                          "model_gb": round(llm.engine.model.nbytes / 1e9, 2)},
                "config": {"workload": ("config4 with shared prefixes: 16 system prompts U[512,2048] x 16 requests, "
@@ -853,7 +860,8 @@ def run_ours(args):
     ext1 = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup, page_size=1)
     dec1 = None if args.no_page1 else measure_decode_page1(dev, args.seed + 31 * rank, args.steps, args.warmup)
     c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps, args.c5_requests)
-    e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, n_requests=args.c4_requests)
+    e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, n_requests=args.c4_requests,
+                                                            fused_proj=not args.no_fused_proj)
     e2e4s = (None if args.no_config4 or args.no_config4_shared else
              measure_e2e_offline(dev, rank, world, args.seed, shared=True, n_requests=args.c4_requests))
 

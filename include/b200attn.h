@@ -306,6 +306,34 @@ int b2a_swiglu(const void* gate_up, int64_t row_stride, void* out, int64_t rows,
 int b2a_rmsnorm(const void* x, int64_t x_row_stride, int64_t x_rows, const int32_t* rows, int64_t n_rows,
                 const void* w, float eps, int H, void* y, int dtype, void* stream);
 
+/* ------------------------------------------------------------------------
+ * Decode-batch projection with its neighbours fused (engine harness).
+ * Replaces, for a step of at most 64 token rows, the projections of a decoder
+ * layer together with the norm in front and the add or activation behind
+ * (python/minisgl_mlx/models/transformer.py: qkv_proj / o_proj :41-42,
+ * gate_up_proj / down_proj :64-65, DecoderLayer.__call__ :80-82, swiglu
+ * :26-30 and :67-69). With W = w [N, K] (row-major, K contiguous) and
+ * xn = x when norm_w is NULL, else the RMSNorm of each x row
+ * (x / sqrt(mean(x^2) + eps) * norm_w):
+ *   mode 0 (plain)     out[M, N]   = xn W^T
+ *   mode 1 (residual)  out[M, N]   = res + xn W^T   (out may be res: in place)
+ *   mode 2 (swiglu)    out[M, N/2] = silu(g) * u,  [g | u] = xn W^T
+ *                      (gate rows 0..N/2-1 of w, up rows N/2..N-1)
+ * bf16 only, fp32 accumulation, one rounding to bf16 per stored value (the
+ * swiglu form rounds g, u and silu(g) like the unfused 16-bit form; the norm's
+ * per-row scale multiplies the fp32 product, so its operand is x * norm_w
+ * rounded once). M <= 64; K a positive multiple of 128; N a multiple of 16
+ * (32 for swiglu). x, w, norm_w 16-byte aligned, x_row_stride a multiple of 8
+ * elements. Launched with programmatic stream serialization: the weight reads
+ * start before the previous kernel of the stream has finished.
+ * ------------------------------------------------------------------------ */
+#define B2A_PROJ_PLAIN 0
+#define B2A_PROJ_RESIDUAL 1
+#define B2A_PROJ_SWIGLU 2
+int b2a_proj(const void* x, int64_t x_row_stride, int M, int K, const void* w, int N, const void* norm_w,
+             float eps, const void* res, int64_t res_row_stride, void* out, int64_t out_row_stride, int mode,
+             int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,6 +9,7 @@
 #include <map>
 #include <mutex>
 #include <string>
+#include <tuple>
 #include <utility>
 #include <vector>
 
@@ -19,6 +20,7 @@
 #include "extend_simt.cuh"
 #include "extend_tc.cuh"
 #include "pack_kv.cuh"
+#include "proj.cuh"
 #include "metadata.cuh"
 #include "rmsnorm.cuh"
 #include "rope_store.cuh"
@@ -920,3 +922,118 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
 }
 
 }  // extern "C"
+
+namespace {
+
+// Projection launch shape: CTAs of `warps` warps, each warp `kpw` 128-wide k
+// slices. The widest split (most warps) whose grid is resident in one wave is
+// taken, so the whole weight stream is in flight at once; residency is the
+// occupancy calculator's, cached per (kernel, warps).
+template <int NB, int A, int MODE, bool NORM>
+int proj_launch(const b2a::ProjArgs& a0, int grid, cudaStream_t st) {
+  // 512-thread CTAs cap a thread at 128 registers, too few for 64 token rows
+  constexpr int MAXW = NB == 8 ? 8 : 16;
+  auto kern = b2a::proj_kernel<NB, A, MODE, NORM, MAXW>;
+  using S = b2a::ProjSmem<NB, A>;
+  const int kc = a0.K / 128;
+  static std::mutex mu;
+  static std::map<std::tuple<int, int, int>, int> resident;  // (device, warps, K) -> CTAs per SM
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return fail(B2A_ERR_CUDA, "proj: no current device");
+  const int sms = num_sms();
+  int warps = 0;
+  for (int wc = std::min(MAXW, kc); wc >= 1; --wc) {
+    if (kc % wc) continue;
+    const size_t smem = S::bytes(a0.K, wc);
+    if (smem > 227 * 1024) continue;
+    if (int rc = ensure_smem((const void*)kern, smem, "proj")) return rc;
+    int per_sm = 0;
+    {
+      std::lock_guard<std::mutex> lock(mu);
+      auto it = resident.find({dev, wc, a0.K});
+      if (it != resident.end()) {
+        per_sm = it->second;
+      } else {
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, wc * 32, smem) != cudaSuccess)
+          return fail(B2A_ERR_CUDA, "proj: occupancy query failed");
+        resident[{dev, wc, a0.K}] = per_sm;
+      }
+    }
+    if (warps == 0 && per_sm > 0) warps = wc;  // the widest split that runs at all
+    if (per_sm > 0 && (int64_t)per_sm * sms >= grid) {
+      warps = wc;
+      break;
+    }
+  }
+  if (warps == 0) return fail(B2A_ERR_UNSUPPORTED, "proj: no launchable warp count for K = %d", a0.K);
+  b2a::ProjArgs a = a0;
+  a.kpw = kc / warps;
+  launch_pdl(kern, dim3((unsigned)grid), dim3(warps * 32), S::bytes(a0.K, warps), st, a);
+  return check_launch("proj_kernel");
+}
+
+template <int NB>
+int proj_tiles(const b2a::ProjArgs& a, int mode, bool norm, int grid, cudaStream_t st) {
+  switch (mode) {
+    case b2a::kProjPlain:
+      return norm ? proj_launch<NB, 1, b2a::kProjPlain, true>(a, grid, st)
+                  : proj_launch<NB, 1, b2a::kProjPlain, false>(a, grid, st);
+    case b2a::kProjResidual:
+      return norm ? proj_launch<NB, 1, b2a::kProjResidual, true>(a, grid, st)
+                  : proj_launch<NB, 1, b2a::kProjResidual, false>(a, grid, st);
+    default:
+      return norm ? proj_launch<NB, 2, b2a::kProjSwiglu, true>(a, grid, st)
+                  : proj_launch<NB, 2, b2a::kProjSwiglu, false>(a, grid, st);
+  }
+}
+
+}  // namespace
+
+extern "C" int b2a_proj(const void* x, int64_t x_row_stride, int M, int K, const void* w, int N,
+                        const void* norm_w, float eps, const void* res, int64_t res_row_stride, void* out,
+                        int64_t out_row_stride, int mode, int dtype, void* stream) {
+  if (M < 0 || K < 0 || N < 0) return fail(B2A_ERR_INVALID, "negative size");
+  if (mode < b2a::kProjPlain || mode > b2a::kProjSwiglu) return fail(B2A_ERR_INVALID, "unknown proj mode %d", mode);
+  if (dtype != B2A_DTYPE_BF16) return fail(B2A_ERR_UNSUPPORTED, "proj: bf16 only (dtype %d)", dtype);
+  if (M == 0 || N == 0) return ok();
+  if (M > 64) return fail(B2A_ERR_UNSUPPORTED, "proj: M = %d token rows (at most 64)", M);
+  if (K == 0 || K % 128) return fail(B2A_ERR_UNSUPPORTED, "proj: K = %d must be a positive multiple of 128", K);
+  const int n_out = mode == b2a::kProjSwiglu ? N / 2 : N;
+  if (mode == b2a::kProjSwiglu ? N % 32 : N % 16)
+    return fail(B2A_ERR_UNSUPPORTED, "proj: N = %d must be a multiple of %d", N, mode == b2a::kProjSwiglu ? 32 : 16);
+  if (!x || !w || !out || (mode == b2a::kProjResidual && !res)) return fail(B2A_ERR_INVALID, "NULL pointer argument");
+  if (!aligned(x, 16) || !aligned(w, 16) || (norm_w && !aligned(norm_w, 16)))
+    return fail(B2A_ERR_INVALID, "proj: x, w and norm_w must be 16-byte aligned");
+  if (!aligned(out, 2) || (res && !aligned(res, 2))) return fail(B2A_ERR_INVALID, "proj: out/res misaligned");
+  if (x_row_stride < K || x_row_stride % 8) return fail(B2A_ERR_INVALID, "proj: x_row_stride %lld (>= K, multiple of 8)",
+                                                       (long long)x_row_stride);
+  if (out_row_stride < n_out) return fail(B2A_ERR_INVALID, "proj: out_row_stride %lld < %d", (long long)out_row_stride, n_out);
+  if (mode == b2a::kProjResidual && res_row_stride < N)
+    return fail(B2A_ERR_INVALID, "proj: res_row_stride %lld < N", (long long)res_row_stride);
+  if (!(eps >= 0.f)) return fail(B2A_ERR_INVALID, "eps must be >= 0");
+  b2a::ProjArgs a;
+  a.x = reinterpret_cast<const __nv_bfloat16*>(x);
+  a.w = reinterpret_cast<const __nv_bfloat16*>(w);
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w);
+  a.res = reinterpret_cast<const __nv_bfloat16*>(res);
+  a.out = reinterpret_cast<__nv_bfloat16*>(out);
+  a.ldx = x_row_stride;
+  a.ldr = res_row_stride;
+  a.ldo = out_row_stride;
+  a.M = M;
+  a.K = K;
+  a.F = N / 2;
+  a.kpw = 0;
+  a.eps = eps;
+  // a CTA holds 16 weight rows (a 16-row gate tile and a 16-row up tile for swiglu)
+  const int A = mode == b2a::kProjSwiglu ? 2 : 1;
+  const int grid = N / (16 * A);
+  if ((size_t)16 * A * (2 * (size_t)K + 64) + 16 > 227 * 1024)
+    return fail(B2A_ERR_UNSUPPORTED, "proj: K = %d: the %d-row weight slab does not fit in shared memory", K, 16 * A);
+  cudaStream_t st = reinterpret_cast<cudaStream_t>(stream);
+  const bool norm = norm_w != nullptr;
+  if (M <= 8) return proj_tiles<1>(a, mode, norm, grid, st);
+  if (M <= 16) return proj_tiles<2>(a, mode, norm, grid, st);
+  if (M <= 32) return proj_tiles<4>(a, mode, norm, grid, st);
+  return proj_tiles<8>(a, mode, norm, grid, st);
+}

@@ -93,6 +93,8 @@ SIGNATURES = {
     ),
     "b2a_swiglu": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, _P]),
     "b2a_rmsnorm": (c_int, [_P, c_int64, c_int64, _P, c_int64, _P, c_float, c_int, _P, c_int, _P]),
+    "b2a_proj": (c_int, [_P, c_int64, c_int, c_int, _P, c_int, _P, c_float, _P, c_int64, _P, c_int64, c_int, c_int,
+                         _P]),
 }
 
 

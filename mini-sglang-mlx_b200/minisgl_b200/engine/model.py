@@ -8,13 +8,18 @@ projection, RMSNorm and a fused gate/up SwiGLU MLP, with residuals; a final
 RMSNorm and tied embeddings as the LM head. Prefill keeps only each
 request's last token before the head (``attn_metadata.last_indices``).
 
-Inputs are packed ``[T]`` token ids. GEMMs are cuBLAS through ``F.linear``;
-the two residual adds of a layer are folded into the o_proj and down GEMMs
-(``torch.addmm`` with beta = 1: one rounding instead of two), and SwiGLU is
-one library kernel (``b2a_swiglu``), as the reference's mx.compile'd
-``swiglu`` is one kernel. The RMSNorms are ``b2a_rmsnorm``; in prefill the
-final norm gathers the last tokens itself (one kernel for the gather and the
-norm). Weights are drawn N(0, 0.02) from a seeded generator (there are no
+Inputs are packed ``[T]`` token ids. A bf16 step of at most 64 tokens (every
+decode step of a rank holding <= 64 requests) runs each layer's projections
+as ``b2a_proj`` launches with their neighbours fused: RMSNorm + qkv_proj,
+o_proj + residual add (in place), RMSNorm + gate_up_proj + SwiGLU, down_proj
++ residual add -- four launches where the unfused form takes seven. Larger
+steps (prefill chunks, big decode batches) and fp32 models use cuBLAS through
+``F.linear``, with the two residual adds folded into the o_proj and down GEMMs
+(``torch.addmm`` with beta = 1: one rounding instead of two), SwiGLU as one
+library kernel (``b2a_swiglu``, as the reference's mx.compile'd ``swiglu`` is
+one kernel) and the RMSNorms as ``b2a_rmsnorm``. In prefill the final norm
+gathers the last tokens itself (one kernel for the gather and the norm).
+Weights are drawn N(0, 0.02) from a seeded generator (there are no
 checkpoints on this machine), norms start at 1.
 """
 
@@ -60,6 +65,31 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, rows: torch.Tensor | 
     nat.call("b2a_rmsnorm", x.data_ptr(), x.stride(0), T, 0 if rows is None else rows.data_ptr(), n, w.data_ptr(),
              float(eps), H, y.data_ptr(), dtype_code(x.dtype), torch.cuda.current_stream().cuda_stream)
     return y
+
+
+PROJ_PLAIN, PROJ_RESIDUAL, PROJ_SWIGLU = 0, 1, 2
+PROJ_MAX_ROWS = 64  # token rows of one b2a_proj launch
+
+
+def proj(x: torch.Tensor, w: torch.Tensor, mode: int, norm_w: torch.Tensor | None = None, eps: float = 0.0,
+         res: torch.Tensor | None = None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``[T, K] x [N, K]^T`` for T <= 64 bf16 rows with the RMSNorm in front (``norm_w``) and
+    the residual add (``PROJ_RESIDUAL``, ``out`` may be ``res``) or SwiGLU (``PROJ_SWIGLU``,
+    ``[T, N/2]``) behind, in one launch (b2a_proj).
+
+    Reference: python/minisgl_mlx/models/transformer.py:80-82 (DecoderLayer.__call__) with the
+    projections of :41-42 and :64-65 and ``swiglu`` of :26-30.
+    """
+    T, K = x.shape
+    N = w.shape[0]
+    assert x.stride(1) == 1 and w.is_contiguous() and w.shape[1] == K
+    if out is None:
+        out = torch.empty((T, N // 2 if mode == PROJ_SWIGLU else N), dtype=x.dtype, device=x.device)
+    nat.call("b2a_proj", x.data_ptr(), x.stride(0), T, K, w.data_ptr(), N,
+             0 if norm_w is None else norm_w.data_ptr(), float(eps), 0 if res is None else res.data_ptr(),
+             0 if res is None else res.stride(0), out.data_ptr(), out.stride(0), mode, dtype_code(x.dtype),
+             torch.cuda.current_stream().cuda_stream)
+    return out
 
 
 @dataclass(frozen=True)
@@ -113,6 +143,10 @@ class Qwen3Model:
         with torch.cuda.device(device):
             self.layers: List[_Layer] = [_Layer(spec, i, gen, dtype, device) for i in range(spec.attn.num_layers)]
         self.norm = torch.ones(spec.hidden_size, dtype=dtype, device=device)
+        # b2a_proj shapes: bf16, K (hidden, heads x head_dim, intermediate) multiples of 128
+        a = spec.attn
+        self.fused_proj = (dtype == torch.bfloat16 and spec.hidden_size % 128 == 0
+                           and (a.num_qo_heads * a.head_dim) % 128 == 0 and spec.intermediate_size % 128 == 0)
 
     @property
     def nbytes(self) -> int:
@@ -128,6 +162,16 @@ class Qwen3Model:
         batch = get_global_ctx().batch
         h = F.embedding(input_ids, self.embed)
         T = h.shape[0]
+        if self.fused_proj and T <= PROJ_MAX_ROWS:
+            for L in self.layers:
+                qkv = proj(h, L.qkv, PROJ_PLAIN, L.in_norm, eps)
+                q = qkv[:, : Hq * D].view(T, Hq, D)
+                k = qkv[:, Hq * D: (Hq + Hkv) * D].view(T, Hkv, D)
+                v = qkv[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+                proj(L.attn(q, k, v, L.q_norm, L.k_norm, eps), L.o, PROJ_RESIDUAL, res=h, out=h)
+                proj(proj(h, L.gate_up, PROJ_SWIGLU, L.post_norm, eps), L.down, PROJ_RESIDUAL, res=h, out=h)
+            h = rms_norm(h, self.norm, eps, batch.attn_metadata.last_indices if batch.is_prefill else None)
+            return F.linear(h, self.embed)
         for L in self.layers:
             x = rms_norm(h, L.in_norm, eps)
             qkv = F.linear(x, L.qkv)

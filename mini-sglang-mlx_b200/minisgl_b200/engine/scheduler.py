@@ -58,6 +58,9 @@ class EngineConfig:
     # keep a device copy of the page table; CUDA-graph decode steps then build their
     # attention metadata on the device, inside the graph (b2a_decode_metadata)
     device_metadata: bool = True
+    # bf16 steps of <= 64 tokens run the layers' projections as b2a_proj launches with the
+    # norms, residual adds and SwiGLU fused in (False: cuBLAS + separate kernels throughout)
+    fused_proj: bool = True
     seed: int = 42
 
 
@@ -68,6 +71,7 @@ class Engine:
         self.dtype = _DTYPES[cfg.dtype]
         a = cfg.spec.attn
         self.model = Qwen3Model(cfg.spec, self.dtype, self.device, seed=cfg.seed)
+        self.model.fused_proj = self.model.fused_proj and cfg.fused_proj
         P = cfg.page_size
         self.num_tokens = cfg.num_tokens // P * P
         self.kv_cache = MHAKVCache(a.num_layers, self.num_tokens, a.num_kv_heads, a.head_dim, self.dtype,

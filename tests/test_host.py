@@ -186,6 +186,35 @@ def test_swiglu_rejects_bad_sizes_before_any_launch():
     nat.call("b2a_swiglu", dummy, 8, dummy, 0, 4, nat.B2A_DTYPE_BF16, None)  # nothing to do
 
 
+def test_proj_rejects_bad_arguments_before_any_launch():
+    dummy = 16  # never dereferenced: every call below fails or returns before a launch
+    bf16 = nat.B2A_DTYPE_BF16
+
+    def call(M=4, K=1024, N=1024, mode=0, dtype=bf16, x_stride=1024, res=0, out_stride=1024):
+        nat.call("b2a_proj", dummy, x_stride, M, K, dummy, N, 0, 1e-6, res, 1024, dummy, out_stride, mode,
+                 dtype, None)
+
+    with pytest.raises(nat.B200AttnError, match="at most 64"):
+        call(M=65)
+    with pytest.raises(nat.B200AttnError, match="multiple of 128"):
+        call(K=1000, x_stride=1000)
+    with pytest.raises(nat.B200AttnError, match="multiple of 16"):
+        call(N=1000)
+    with pytest.raises(nat.B200AttnError, match="multiple of 32"):
+        call(N=1040, mode=2)
+    with pytest.raises(nat.B200AttnError, match="bf16 only"):
+        call(dtype=nat.B2A_DTYPE_F32)
+    with pytest.raises(ValueError, match="unknown proj mode"):
+        call(mode=3)
+    with pytest.raises(ValueError, match="NULL"):
+        call(mode=1)  # residual without res
+    with pytest.raises(ValueError, match="x_row_stride"):
+        call(x_stride=1020)
+    with pytest.raises(ValueError, match="negative"):
+        call(M=-1)
+    call(M=0)  # nothing to do
+
+
 def test_extend_executed_flops_counts_whole_tiles_and_blocks():
     """bench.extend_executed_flops against a brute-force walk of the tcgen05 kernel's
     work: items of two 128/G-token tiles, each over whole 128-key blocks up to the last
