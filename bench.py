@@ -340,7 +340,7 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
     warm-up generation. Under torchrun the requests are partitioned by the
     prefix-affinity router (engine/router.py: first-page groups, placed
     longest-first) and the job throughput is all outputs / slowest rank.
-    Decode steps of <= 64 requests run the layers' projections as b2a_proj
+    Decode steps of <= 32 requests run the layers' projections as b2a_proj
     launches (norm, residual adds and SwiGLU fused) unless ``fused_proj`` is off.
     """
     import time
@@ -410,7 +410,7 @@ def measure_e2e_offline(dev, rank: int, world: int, seed: int, shared: bool = Fa
                          "prefill_steps": llm.num_steps["prefill"], "decode_steps": llm.num_steps["decode"],
                          "gpu_ms_per_decode_step": round(1e3 * llm.timing["gpu_decode"] / max(1, llm.num_steps["decode"]), 4),
                          "time_s": {k: round(v, 3) for k, v in llm.timing.items()},
-                         "fused_proj_steps_le_64": llm.engine.model.fused_proj,
+                         "fused_proj_steps_le_32": llm.engine.model.fused_proj,
                          "kv_pool_gb": round(llm.engine.kv_cache.nbytes / 1e9, 2),
                          "model_gb": round(llm.engine.model.nbytes / 1e9, 2)},
                "config": {"workload": ("config4 with shared prefixes: 16 system prompts U[512,2048] x 16 requests, "

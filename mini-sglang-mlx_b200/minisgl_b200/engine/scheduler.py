@@ -58,7 +58,7 @@ class EngineConfig:
     # keep a device copy of the page table; CUDA-graph decode steps then build their
     # attention metadata on the device, inside the graph (b2a_decode_metadata)
     device_metadata: bool = True
-    # bf16 steps of <= 64 tokens run the layers' projections as b2a_proj launches with the
+    # bf16 steps of <= 32 tokens run the layers' projections as b2a_proj launches with the
     # norms, residual adds and SwiGLU fused in (False: cuBLAS + separate kernels throughout)
     fused_proj: bool = True
     seed: int = 42
