@@ -456,12 +456,17 @@ def extend_executed_flops(prefix: np.ndarray, extend: np.ndarray, Hq: int, Hkv: 
     return float(blocks) * Hkv * 2 * (2 * 128 * KB * D)
 
 
-def measure_extend(dev, seed: int, steps: int, warmup: int, page_size: int | None = None):
+def measure_extend(dev, seed: int, steps: int, warmup: int, page_size: int | None = None,
+                   allocator_order: bool = False):
     """Config 3: 32 ragged requests with a cached radix prefix, fused RoPE+store then extend attention.
 
     page_size None is config 3's page size 16 (the tcgen05 kernel reads the pool directly);
-    page_size 1 is the reference's default: the backend packs each request's KV rows into
-    16-slot pages (b2a_pack_kv) and runs the same kernel on them, both inside the timed call.
+    page_size 1 is the reference's default: the tcgen05 kernel reads the keys in groups of
+    16 (b2a_extend_groups), each group in place when its slots are one run of consecutive
+    slots, else from a staging pool the backend packs it into (b2a_pack_kv), both inside
+    the timed call. The page-size-1 slots are a seeded random permutation (every group
+    packed, the worst case) or, with ``allocator_order``, what a fresh free list hands out
+    (scheduler/cache.py:28-72): every prefix one run, then every request's new tokens one run.
     """
     import torch
 
@@ -475,6 +480,15 @@ def measure_extend(dev, seed: int, steps: int, warmup: int, page_size: int | Non
     Hq, Hkv, D = cfg.num_qo_heads, cfg.num_kv_heads, cfg.head_dim
     eb = W.config3_batch(seed=seed, page_size=page_size)
     pb = eb.paged
+    if allocator_order:
+        assert pb.page_size == 1
+        off = 0
+        for b, L in enumerate(eb.prefix.tolist()):
+            pb.page_table[b, :L] = np.arange(off, off + L, dtype=np.int32)
+            off += L
+        for b, (Lp, Le) in enumerate(zip(eb.prefix.tolist(), eb.extend.tolist())):
+            pb.page_table[b, Lp:Lp + Le] = np.arange(off, off + Le, dtype=np.int32)
+            off += Le
     kv = MHAKVCache(1, pb.num_slots, Hkv, D, torch.bfloat16, device=dev)
     gen = torch.Generator(device=dev).manual_seed(seed)
     kv.k[0].normal_(generator=gen)
@@ -527,6 +541,9 @@ def measure_extend(dev, seed: int, steps: int, warmup: int, page_size: int | Non
 
     tile = nat.extend_tile_q(Hq, Hkv, D, nat.B2A_DTYPE_BF16, max(pb.page_size, 16))
     tc = tile == 2 * (128 // (Hq // Hkv))
+    packed_share = None
+    if meta.group_starts:  # share of the 16-key groups copied to the staging pool
+        packed_share = round((meta.pack.n_groups if meta.pack is not None else 0) / max(1, int(meta.kv_indices.numel())), 4)
     # tile-padded work the tensor cores run (partial query tiles, masked key blocks)
     exe = extend_executed_flops(eb.prefix, eb.extend, Hq, Hkv, D) if tc else None
     return {"metric": "extend attention TFLOP/s (causal, visible keys only)", "value": round(tf, 2),
@@ -539,8 +556,11 @@ def measure_extend(dev, seed: int, steps: int, warmup: int, page_size: int | Non
                          "frac": round(tf / peak, 4), "peak_kind": kind + " (bf16 dense, burst)"},
             "config": {"workload": "config3: 32 ragged requests, prefix U[0,4096] page-aligned (+1 unaligned), "
                                    f"extend U[64,512], 16q/8kv/128, bf16, page {pb.page_size}, RoPE theta 1e6 fused store"
-                                   + (" (KV rows packed into 16-slot pages inside the timed call)" if pb.page_size < 16 else ""),
+                                   + ((" (16-key groups: runs read in place, the rest packed to a staging pool inside "
+                                       "the timed call; slots " + ("in allocator order)" if allocator_order
+                                                                    else "a random permutation)")) if pb.page_size < 16 else ""),
                        "tokens": T, "sum_prefix": int(eb.prefix.sum()), "tile_q_tokens": tile,
+                       "packed_group_share": packed_share,
                        "kernel": "extend_tc2_kernel (tcgen05, 2 x 128-row tiles)" if tile == 2 * (128 // (Hq // Hkv)) else "extend_simt_kernel"},
             # config 3': the fused RoPE + KV store of the same T tokens (HBM-bound)
             "rope_store_config3p": {"metric": "fused RoPE + KV store HBM GB/s", "value": round(rope_bytes / (rope_ms * 1e-3) / 1e9, 1),
@@ -858,6 +878,10 @@ def run_ours(args):
     torch.cuda.empty_cache()
     ext = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup)
     ext1 = None if args.no_extend else measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup, page_size=1)
+    if ext1 is not None:
+        ea = measure_extend(dev, args.seed + 31 * rank, args.steps, args.warmup, page_size=1, allocator_order=True)
+        ext1["allocator_order"] = {k: ea[k] for k in ("value", "ms_per_call", "roofline", "clocks")}
+        ext1["allocator_order"]["packed_group_share"] = ea["config"]["packed_group_share"]
     dec1 = None if args.no_page1 else measure_decode_page1(dev, args.seed + 31 * rank, args.steps, args.warmup)
     c5 = None if args.no_config5 else measure_config5(dev, rank, world, args.seed, args.steps, args.c5_requests)
     e2e4 = None if args.no_config4 else measure_e2e_offline(dev, rank, world, args.seed, n_requests=args.c4_requests,

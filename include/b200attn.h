@@ -257,6 +257,30 @@ int b2a_decode_noalloc(const void* q, const void* k_pool, const void* v_pool, in
 int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* tile_q);
 
 /* ------------------------------------------------------------------------
+ * Extend attention over 16-key groups that start at any slot (pools with
+ * page_size < 16, e.g. the reference's default page_size 1).
+ * Same attention as b2a_extend (attention/base.py:70-105), with the keys of
+ * request b given as groups of 16: group j covers keys [16j, 16j + 16) and
+ * its rows are 16 consecutive slots starting at
+ *   e = group_starts[group_indptr[b] + j]:
+ *   e < num_slots                    -> k_pool / v_pool rows e .. e + 15
+ *   num_slots <= e < num_slots + stage_slots
+ *                                    -> k_stage / v_stage rows e - num_slots ..
+ * Lkv_b = 16 * (groups_b - 1) + kv_last_len[b]; rows of a group past Lkv_b
+ * (or past a pool's end) are never attended. A caller reads runs of
+ * contiguous slots in place and copies only the other groups to the staging
+ * pool (b2a_pack_kv with one 16-row page per group). work comes from
+ * b2a_extend_plan(qo_indptr, group_indptr, kv_last_len, B, 16, tile_q, ...).
+ * bf16, D 128, GQA group 1/2/4/8 (the tcgen05 kernel) only. A start outside
+ * both pools zero-fills its group and records device error 32.
+ * ------------------------------------------------------------------------ */
+int b2a_extend_groups(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                      const void* k_stage, const void* v_stage, int64_t stage_slots,
+                      const int32_t* qo_indptr, const int32_t* group_indptr, const int32_t* group_starts,
+                      const int32_t* kv_last_len, const int32_t* work, int n_work, int T, int B, int Hq,
+                      int Hkv, int D, float scale, void* out, int dtype, void* stream);
+
+/* ------------------------------------------------------------------------
  * Pack requests' KV rows into pages of 16 contiguous slots (no reference
  * counterpart: it lets b2a_extend run its tcgen05 path for pools whose page
  * size is below 16, e.g. the reference's default page_size 1).
@@ -265,6 +289,10 @@ int b2a_extend_tile_q(int Hq, int Hkv, int D, int dtype, int page_size, int* til
  *   k_out[out_page_indptr[b] * 16 + p] = k_pool[src]   (whole Hkv x D rows, bytes)
  *   v_out[...]                        = v_pool[src]
  * total_tokens = tok_indptr[B]; k_out / v_out hold out_slots rows.
+ * Row-list form: tok_indptr, kv_indptr and out_page_indptr NULL, page_size 1:
+ *   k_out[g] = k_pool[kv_indices[g]], v_out[g] = v_pool[kv_indices[g]],  g < total_tokens
+ * (the groups b2a_extend_groups reads from its staging pool; B is ignored but > 0).
+ * A source outside the pool is skipped and recorded as device error 32.
  * ------------------------------------------------------------------------ */
 int b2a_pack_kv(const void* k_pool, const void* v_pool, int64_t num_slots, const int32_t* kv_indptr,
                 const int32_t* kv_indices, int page_size, const int32_t* tok_indptr,

@@ -725,12 +725,16 @@ int b2a_pack_kv(const void* k_pool, const void* v_pool, int64_t num_slots, const
                 void* stream) {
   if (B < 0 || total_tokens < 0) return fail(B2A_ERR_INVALID, "negative size");
   if (B == 0 || total_tokens == 0) return ok();
+  const bool row_list = tok_indptr == nullptr;
+  if (row_list && (kv_indptr || out_page_indptr || page_size != 1))
+    return fail(B2A_ERR_INVALID, "row-list pack: kv_indptr and out_page_indptr NULL, page_size 1");
+  if (row_list && total_tokens > out_slots) return fail(B2A_ERR_INVALID, "row-list pack: total_tokens > out_slots");
   const size_t es = dtype_size(dtype);
   if (es == 0) return fail(B2A_ERR_UNSUPPORTED, "dtype %d", dtype);
   if (Hkv <= 0 || D <= 0) return fail(B2A_ERR_INVALID, "bad head shape");
   const size_t row = (size_t)Hkv * D * es;
   if (row % 16) return fail(B2A_ERR_INVALID, "token rows of %zu bytes are not a multiple of 16", row);
-  if (!k_pool || !v_pool || !kv_indptr || !kv_indices || !tok_indptr || !out_page_indptr || !k_out || !v_out)
+  if (!k_pool || !v_pool || !kv_indices || !k_out || !v_out || (!row_list && (!kv_indptr || !out_page_indptr)))
     return fail(B2A_ERR_INVALID, "NULL pointer argument");
   if (!aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(k_out, 16) || !aligned(v_out, 16))
     return fail(B2A_ERR_INVALID, "pools must be 16-byte aligned");
@@ -886,8 +890,8 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
   const int G = Hq / Hkv;
   if (extend_uses_tc(Hq, Hkv, D, dtype, plog)) {
     if (int rc = ensure_smem((const void*)b2a::extend_tc2_kernel, b2a::Tc2Smem::ALLOC, "extend_tc")) return rc;
-    return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, qo_indptr, kv_indptr, kv_indices, kv_last_page_len,
-                                 plog, work, n_work, T, Hq, Hkv, scale, out, st, g_err);
+    return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, nullptr, nullptr, 0, 0, qo_indptr, kv_indptr,
+                                 kv_indices, kv_last_page_len, plog, work, n_work, T, Hq, Hkv, scale, out, st, g_err);
   }
   if (G > b2a::kSimtRows) return fail(B2A_ERR_UNSUPPORTED, "GQA group %d too large", G);
   b2a::ExtendArgs a;
@@ -919,6 +923,30 @@ int b2a_extend(const void* q, const void* k_pool, const void* v_pool, int64_t nu
       });
     });
   });
+}
+
+int b2a_extend_groups(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots, const void* k_stage,
+                      const void* v_stage, int64_t stage_slots, const int32_t* qo_indptr, const int32_t* group_indptr,
+                      const int32_t* group_starts, const int32_t* kv_last_len, const int32_t* work, int n_work, int T,
+                      int B, int Hq, int Hkv, int D, float scale, void* out, int dtype, void* stream) {
+  if (n_work < 0 || B < 0 || T < 0 || stage_slots < 0) return fail(B2A_ERR_INVALID, "negative size");
+  if (n_work == 0) return ok();
+  if (int rc = check_heads(Hq, Hkv, D)) return rc;
+  if (!extend_uses_tc(Hq, Hkv, D, dtype, 4))
+    return fail(B2A_ERR_UNSUPPORTED, "extend_groups: the tcgen05 path only (bf16, D 128, GQA group 1/2/4/8)");
+  if (!q || !k_pool || !v_pool || !qo_indptr || !group_indptr || !group_starts || !work || !out ||
+      (stage_slots > 0 && (!k_stage || !v_stage)))
+    return fail(B2A_ERR_INVALID, "NULL pointer argument");
+  if (!aligned(work, 16)) return fail(B2A_ERR_INVALID, "work must be 16-byte aligned (read as int4)");
+  if (!aligned(q, 16) || !aligned(k_pool, 16) || !aligned(v_pool, 16) || !aligned(out, 16) ||
+      (stage_slots > 0 && (!aligned(k_stage, 16) || !aligned(v_stage, 16))))
+    return fail(B2A_ERR_INVALID, "q/pools/out must be 16-byte aligned");
+  if (num_slots <= 0 || num_slots + stage_slots > 0x7fffffffLL - 64)
+    return fail(B2A_ERR_INVALID, "num_slots + stage_slots must be in (0, 2^31)");
+  if (int rc = ensure_smem((const void*)b2a::extend_tc2_kernel, b2a::Tc2Smem::ALLOC, "extend_tc")) return rc;
+  return b2a::extend_tc_launch(q, k_pool, v_pool, num_slots, k_stage, v_stage, stage_slots, 1, qo_indptr,
+                               group_indptr, group_starts, kv_last_len, 4, work, n_work, T, Hq, Hkv, scale, out,
+                               reinterpret_cast<cudaStream_t>(stream), g_err);
 }
 
 }  // extern "C"

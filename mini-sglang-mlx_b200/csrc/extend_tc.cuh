@@ -43,7 +43,9 @@ struct TcArgs {
   const int32_t* work;
   __nv_bfloat16* out;
   int64_t num_slots;
+  int64_t stage_slots;  // rows of the staging pool (group-start mode)
   int page_log2;
+  int group_starts;     // kv_indices hold each 16-key group's first slot, not page ids
   int Hq, G;
   float qscale;  // scale * log2(e)
 };
@@ -226,7 +228,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
 
 __global__ void __launch_bounds__(kTc2Threads, 1)
     extend_tc2_kernel(const __grid_constant__ CUtensorMap qmap, const __grid_constant__ CUtensorMap kmap,
-                      const __grid_constant__ CUtensorMap vmap, const TcArgs a) {
+                      const __grid_constant__ CUtensorMap vmap, const __grid_constant__ CUtensorMap kmap2,
+                      const __grid_constant__ CUtensorMap vmap2, const TcArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + Tc2Smem::BARS);
@@ -307,14 +310,28 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
       const int st = j & 1;
       const uint32_t ph = (uint32_t)(j >> 1) & 1u;
       int z = (int)a.num_slots;  // out of range -> zero fill
+      bool staged = false;       // this lane's group comes from the staging pool
       const int b = lane >> 1, half = lane & 1;
       if (lane < 16) {
         const int key0 = j * kTcKeys + b * 16;
         if (key0 < Lkv) {
-          const int64_t page = a.kv_indices[pbeg + (key0 >> a.page_log2)];
-          const int64_t slot = page * P + (key0 & (P - 1));
-          if (page >= 0 && slot + 16 <= a.num_slots) z = (int)slot;
-          else watchdog_set(kWdBadSlot);
+          const int64_t e = a.kv_indices[pbeg + (key0 >> a.page_log2)];
+          if (a.group_starts) {
+            // the group's 16 rows start at slot e of the pool, or at e - num_slots of the
+            // staging pool; rows past a pool's end load as zeros (keys past Lkv are masked)
+            if (e >= 0 && e < a.num_slots) {
+              z = (int)e;
+            } else if (e >= a.num_slots && e - a.num_slots < a.stage_slots) {
+              z = (int)(e - a.num_slots);
+              staged = true;
+            } else {
+              watchdog_set(kWdBadSlot);
+            }
+          } else {
+            const int64_t slot = e * P + (key0 & (P - 1));
+            if (e >= 0 && slot + 16 <= a.num_slots) z = (int)slot;
+            else watchdog_set(kWdBadSlot);
+          }
         }
       }
       bool ok = __all_sync(0xffffffffu, tc_wait(&k_empty[st], ph ^ 1u, abort_flag));
@@ -322,16 +339,16 @@ __global__ void __launch_bounds__(kTc2Threads, 1)
       if (lane == 0) mbar_arrive_expect_tx(&k_full[st], kTcTileBytes);
       __syncwarp();
       if (lane < 16)
-        tma_load_3d(smem + Tc2Smem::K0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &kmap, half * 64, h, z,
-                    &k_full[st]);
+        tma_load_3d(smem + Tc2Smem::K0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, staged ? &kmap2 : &kmap,
+                    half * 64, h, z, &k_full[st]);
       ++issued_k;
       ok = __all_sync(0xffffffffu, tc_wait(&v_empty[st], ph ^ 1u, abort_flag));
       if (!ok) break;
       if (lane == 0) mbar_arrive_expect_tx(&v_full[st], kTcTileBytes);
       __syncwarp();
       if (lane < 16)
-        tma_load_3d(smem + Tc2Smem::V0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, &vmap, half * 64, h, z,
-                    &v_full[st]);
+        tma_load_3d(smem + Tc2Smem::V0 + st * kTcTileBytes + half * kTcHalfBytes + b * 2048, staged ? &vmap2 : &vmap,
+                    half * 64, h, z, &v_full[st]);
       ++issued_v;
     }
     if (lane == 0) {
@@ -620,6 +637,7 @@ inline bool encode_3d(PFN_cuTensorMapEncodeTiled_v12000 enc, CUtensorMap* map, c
 }
 
 inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_pool, int64_t num_slots,
+                            const void* k_stage, const void* v_stage, int64_t stage_slots, int group_starts,
                             const int32_t* qo_indptr, const int32_t* kv_indptr, const int32_t* kv_indices,
                             const int32_t* kv_last_page_len, int page_log2, const int32_t* work, int n_work, int T,
                             int Hq, int Hkv, float scale, void* out, cudaStream_t st, std::string& err) {
@@ -630,13 +648,21 @@ inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_poo
     err = "extend_tc: T and num_slots must be in (0, 2^31)";
     return 1;
   }
-  CUtensorMap qm, km, vm;
+  CUtensorMap qm, km, vm, km2, vm2;
   const uint64_t row = (uint64_t)kTcD * 2;
   if (!encode_3d(enc, &qm, q, kTcD, (uint64_t)Hq, (uint64_t)T, row, row * Hq, 64, (uint32_t)G,
                  (uint32_t)(kTcRows / G)) ||
       !encode_3d(enc, &km, k_pool, kTcD, (uint64_t)Hkv, (uint64_t)num_slots, row, row * Hkv, 64, 1, 16) ||
       !encode_3d(enc, &vm, v_pool, kTcD, (uint64_t)Hkv, (uint64_t)num_slots, row, row * Hkv, 64, 1, 16)) {
     err = "extend_tc: cuTensorMapEncodeTiled rejected a tensor map";
+    return 1;
+  }
+  km2 = km;
+  vm2 = vm;
+  if (stage_slots > 0 &&
+      (!encode_3d(enc, &km2, k_stage, kTcD, (uint64_t)Hkv, (uint64_t)stage_slots, row, row * Hkv, 64, 1, 16) ||
+       !encode_3d(enc, &vm2, v_stage, kTcD, (uint64_t)Hkv, (uint64_t)stage_slots, row, row * Hkv, 64, 1, 16))) {
+    err = "extend_tc: cuTensorMapEncodeTiled rejected the staging tensor map";
     return 1;
   }
   TcArgs a;
@@ -647,7 +673,9 @@ inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_poo
   a.work = work;
   a.out = reinterpret_cast<__nv_bfloat16*>(out);
   a.num_slots = num_slots;
+  a.stage_slots = stage_slots > 0 ? stage_slots : 0;
   a.page_log2 = page_log2;
+  a.group_starts = group_starts;
   a.Hq = Hq;
   a.G = G;
   a.qscale = scale * kLog2e;
@@ -658,7 +686,8 @@ inline int extend_tc_launch(const void* q, const void* k_pool, const void* v_poo
   // y is limited to 65535, so longer work lists go out in chunks.
   for (int off = 0; off < n_work; off += 65535) {
     a.work = work + 4 * (size_t)off;
-    extend_tc2_kernel<<<dim3(Hkv, std::min(65535, n_work - off)), kTc2Threads, Tc2Smem::ALLOC, st>>>(qm, km, vm, a);
+    extend_tc2_kernel<<<dim3(Hkv, std::min(65535, n_work - off)), kTc2Threads, Tc2Smem::ALLOC, st>>>(qm, km, vm, km2,
+                                                                                                       vm2, a);
   }
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) {

@@ -8,6 +8,9 @@
 // runs the tcgen05 kernel on that pool with identity page ids. One warp per
 // token row (all kv heads: Hkv * D * sizeof(T) bytes) copies K and V with
 // 16-byte vector loads; the copy is byte-exact.
+// Row-list form (tok_indptr == NULL): row g < total copies slot kv_indices[g]
+// of the pool to staging row g -- the 16-key groups of extend_groups that are
+// not one run of consecutive slots, each padded to 16 rows by its caller.
 #pragma once
 #include "common.cuh"
 
@@ -36,19 +39,26 @@ __global__ void __launch_bounds__(256) pack_kv_kernel(PackArgs a) {
   const int lane = threadIdx.x & 31;
   const int64_t g = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   if (g >= a.total) return;
-  // request of row g: last b with tok_indptr[b] <= g
-  int lo = 0, hi = a.B - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (a.tok_indptr[mid] <= g) lo = mid;
-    else hi = mid - 1;
+  int64_t page, src, dst;
+  if (a.tok_indptr == nullptr) {  // row list
+    page = a.kv_indices[g];
+    src = page;
+    dst = g;
+  } else {
+    // request of row g: last b with tok_indptr[b] <= g
+    int lo = 0, hi = a.B - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.tok_indptr[mid] <= g) lo = mid;
+      else hi = mid - 1;
+    }
+    const int b = lo;
+    const int64_t p = g - a.tok_indptr[b];
+    const int P = 1 << a.page_log2;
+    page = a.kv_indices[a.kv_indptr[b] + (p >> a.page_log2)];
+    src = page * P + (p & (P - 1));
+    dst = (int64_t)a.out_page_indptr[b] * kPackPage + p;
   }
-  const int b = lo;
-  const int64_t p = g - a.tok_indptr[b];
-  const int P = 1 << a.page_log2;
-  const int64_t page = a.kv_indices[a.kv_indptr[b] + (p >> a.page_log2)];
-  const int64_t src = page * P + (p & (P - 1));
-  const int64_t dst = (int64_t)a.out_page_indptr[b] * kPackPage + p;
   if (page < 0 || src >= a.num_slots || dst >= a.out_slots) {
     if (lane == 0) watchdog_set(kWdBadSlot);
     return;

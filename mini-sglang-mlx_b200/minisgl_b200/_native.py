@@ -91,6 +91,11 @@ SIGNATURES = {
         [_P, _P, _P, c_int64, _P, _P, _P, _P, c_int, _P, c_int, c_int, c_int, c_int, c_int, c_int,
          c_float, _P, c_int, _P],
     ),
+    "b2a_extend_groups": (
+        c_int,
+        [_P, _P, _P, c_int64, _P, _P, c_int64, _P, _P, _P, _P, _P, c_int, c_int, c_int, c_int, c_int, c_int,
+         c_float, _P, c_int, _P],
+    ),
     "b2a_swiglu": (c_int, [_P, c_int64, _P, c_int64, c_int, c_int, _P]),
     "b2a_rmsnorm": (c_int, [_P, c_int64, c_int64, _P, c_int64, _P, c_float, c_int, _P, c_int, _P]),
     "b2a_proj": (c_int, [_P, c_int64, c_int, c_int, _P, c_int, _P, c_float, _P, c_int64, _P, c_int64, c_int, c_int,

@@ -56,21 +56,21 @@ class B200PrefillMetadata:
     n_work: int
     total_q: int
     page_size: int
-    # set when the pool's page size is below what the tcgen05 extend needs: the
-    # requests' KV rows are packed into 16-slot pages first (b2a_pack_kv) and
-    # kv_indptr / kv_indices / kv_last_page_len above describe that packed pool
+    # set when the pool's page size is below what the tcgen05 extend needs: kv_indptr /
+    # kv_indices / kv_last_page_len are then a CSR of 16-key groups and their first slots
+    # (b2a_extend_groups); groups that are not one run of consecutive slots are packed
+    # into a staging pool first (b2a_pack_kv) and their starts point there (>= num_slots)
     pack: "PackPlan | None" = None
+    group_starts: bool = False
 
 
 @dataclass
 class PackPlan:
-    src_kv_indptr: torch.Tensor  # int32 [B+1] page CSR of the real pool (device)
-    src_kv_indices: torch.Tensor  # int32 page ids of the real pool (device)
-    src_page_size: int
-    tok_indptr: torch.Tensor  # int32 [B+1] token CSR (device)
-    out_page_indptr: torch.Tensor  # int32 [B+1] first packed page of each request (device)
-    total_tokens: int
-    out_slots: int
+    """b2a_pack_kv row list: one 16-row staging page per group that is not a run."""
+
+    src_kv_indices: torch.Tensor  # int32 [16 n] source slot of every staging row (device)
+    n_groups: int
+    out_slots: int  # 16 n
 
 
 def _page_size() -> int:
@@ -239,9 +239,9 @@ class B200AttnBackend(BaseAttnBackend):
         tile_q = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code, P)
         if P < self.PACK_PAGE:
             tile16 = nat.extend_tile_q(self.Hq, self.Hkv, self.D, self.dtype_code, self.PACK_PAGE)
-            if tile16 != tile_q:  # the tensor-core kernel takes this shape once pages are 16 slots
-                return self._packed_extend_metadata(qo_indptr, np.asarray(lens, dtype=np.int64), kv_indptr,
-                                                    kv_indices, P, tile16)
+            if tile16 != tile_q:  # the tensor-core kernel takes this shape in groups of 16 keys
+                return self._grouped_extend_metadata(qo_indptr, np.asarray(lens, dtype=np.int64), kv_indptr,
+                                                     kv_indices, P, tile16)
         work = nat.extend_plan(qo_indptr, kv_indptr, lpl, P, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
         dev = self._stager.upload([last_indices, qo_indptr, kv_indptr, kv_indices, lpl, work], self.device)
@@ -253,31 +253,64 @@ class B200AttnBackend(BaseAttnBackend):
 
     PACK_PAGE = 16
 
-    def _packed_extend_metadata(self, qo_indptr, lens, src_indptr, src_indices, P, tile_q) -> B200PrefillMetadata:
-        """Metadata for extend over a packed pool: request b's Lkv rows at slots
-        out_page_indptr[b] * 16 + [0, Lkv), pages of 16 with identity ids."""
+    def _grouped_extend_metadata(self, qo_indptr, lens, src_indptr, src_indices, P, tile_q) -> B200PrefillMetadata:
+        """Extend metadata for a pool whose page size is below 16: request b's keys in groups
+        of 16 (b2a_extend_groups). A group whose 16 rows are one run of consecutive slots
+        (what a fresh free list hands a prompt) is read in place: its start is its first
+        slot. The other groups are packed into 16-row pages of a staging pool
+        (b2a_pack_kv, one page per group) and start at num_slots + 16 * page."""
         Q = self.PACK_PAGE
         B = len(lens)
+        lens = np.asarray(lens, dtype=np.int64)
         tok_indptr = np.zeros(B + 1, np.int64)
         np.cumsum(lens, out=tok_indptr[1:])
-        npages = (lens + Q - 1) // Q
-        out_page_indptr = np.zeros(B + 1, np.int32)
-        np.cumsum(npages, out=out_page_indptr[1:])
-        total_pages = int(out_page_indptr[-1])
-        kv_indices = np.arange(total_pages, dtype=np.int32)
-        lpl = np.where(npages > 0, lens - (npages - 1) * Q, 0).astype(np.int32)
-        work = nat.extend_plan(qo_indptr, out_page_indptr, lpl, Q, tile_q)
+        T_kv = int(tok_indptr[-1])
+        if T_kv >= 2 ** 31:
+            raise ValueError("grouped extend: more than 2^31 KV rows in one batch")
+        req = np.repeat(np.arange(B), lens)
+        pos = np.arange(T_kv, dtype=np.int64) - tok_indptr[req]
+        src_indptr = np.asarray(src_indptr, dtype=np.int64)
+        src_indices = np.asarray(src_indices, dtype=np.int64)
+        tok = src_indices[src_indptr[req] + pos // P] * P + pos % P  # slot of every key, in key order
+        ngroups = (lens + Q - 1) // Q
+        group_indptr = np.zeros(B + 1, np.int64)
+        np.cumsum(ngroups, out=group_indptr[1:])
+        G = int(group_indptr[-1])
+        gid = group_indptr[req] + pos // Q
+        gfirst = np.zeros(G, np.int64)  # key index of each group's first key
+        gfirst[gid[pos % Q == 0]] = np.nonzero(pos % Q == 0)[0]
+        num_slots = self.kv_cache.num_tokens
+        greq = np.repeat(np.arange(B), ngroups)
+        glen_all = np.minimum(Q, lens[greq] - Q * (np.arange(G) - group_indptr[greq]))
+        run_ok = tok == tok[gfirst[gid]] + pos % Q
+        group_ok = np.logical_and.reduceat(run_ok, gfirst) if G else np.zeros(0, bool)
+        # a run is read in place only inside the pool: any other slot goes through the
+        # packer, whose bounds check reports it (a start >= num_slots means the staging pool)
+        group_ok &= (tok[gfirst] >= 0) & (tok[gfirst] + glen_all <= num_slots)
+        packed = np.nonzero(~group_ok)[0]
+        n_packed = len(packed)
+        starts = np.where(group_ok, tok[gfirst] if G else 0, 0).astype(np.int64)
+        starts[packed] = num_slots + Q * np.arange(n_packed, dtype=np.int64)
+        if G and starts.max() >= 2 ** 31:
+            raise ValueError("grouped extend: staging slots past 2^31")
+        lpl = np.where(ngroups > 0, lens - (ngroups - 1) * Q, 0).astype(np.int32)
+        group_indptr32 = group_indptr.astype(np.int32)
+        work = nat.extend_plan(qo_indptr, group_indptr32, lpl, Q, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
-        if int(tok_indptr[-1]) >= 2 ** 31:
-            raise ValueError("packed extend: more than 2^31 KV rows in one batch")
-        dev = self._stager.upload([last_indices, qo_indptr, out_page_indptr, kv_indices, lpl, work, src_indptr,
-                                   src_indices, tok_indptr.astype(np.int32)], self.device)
-        pack = PackPlan(src_kv_indptr=dev[6], src_kv_indices=dev[7], src_page_size=P, tok_indptr=dev[8],
-                        out_page_indptr=dev[2], total_tokens=int(tok_indptr[-1]), out_slots=max(total_pages * Q, Q))
+        arrays = [last_indices, qo_indptr, group_indptr32, starts.astype(np.int32), lpl, work]
+        pack = None
+        if n_packed:
+            # the packed groups' source slots as a row list of 16 per group (staging row
+            # 16 k + i); a short last group repeats its last slot in rows nobody attends
+            rows16 = gfirst[packed][:, None] + np.minimum(np.arange(Q)[None, :], glen_all[packed][:, None] - 1)
+            arrays.append(tok[rows16.reshape(-1)].astype(np.int32))
+        dev = self._stager.upload(arrays, self.device)
+        if n_packed:
+            pack = PackPlan(src_kv_indices=dev[6], n_groups=n_packed, out_slots=Q * n_packed)
         return B200PrefillMetadata(
             last_indices=dev[0], q_offsets=qo_indptr.tolist(), qo_indptr=dev[1], kv_indptr=dev[2],
             kv_indices=dev[3], kv_last_page_len=dev[4], work=dev[5].view(-1, 4), n_work=int(work.shape[0]),
-            total_q=int(qo_indptr[-1]), page_size=Q, pack=pack,
+            total_q=int(qo_indptr[-1]), page_size=Q, pack=pack, group_starts=True,
         )
 
     def _stage_for(self, slots: int):
@@ -301,16 +334,26 @@ class B200AttnBackend(BaseAttnBackend):
         B = len(meta.q_offsets) - 1
         k_pool, v_pool = self.kv_cache.k_cache(layer_id), self.kv_cache.v_cache(layer_id)
         num_slots = self.kv_cache.num_tokens
-        if meta.pack is not None:
-            pk = meta.pack
-            k_st, v_st = self._stage_for(pk.out_slots)
+        if meta.group_starts:
+            k_st = v_st = None
+            stage_slots = 0
+            if meta.pack is not None:
+                pk = meta.pack
+                k_st, v_st = self._stage_for(pk.out_slots)
+                stage_slots = pk.out_slots
+                nat.call(
+                    "b2a_pack_kv", k_pool.data_ptr(), v_pool.data_ptr(), num_slots, None,
+                    pk.src_kv_indices.data_ptr(), 1, None, None, pk.n_groups, pk.out_slots, self.Hkv, self.D,
+                    self.dtype_code, k_st.data_ptr(), v_st.data_ptr(), pk.out_slots, current_stream_ptr(self.device),
+                )
             nat.call(
-                "b2a_pack_kv", k_pool.data_ptr(), v_pool.data_ptr(), num_slots, pk.src_kv_indptr.data_ptr(),
-                pk.src_kv_indices.data_ptr(), pk.src_page_size, pk.tok_indptr.data_ptr(),
-                pk.out_page_indptr.data_ptr(), B, pk.total_tokens, self.Hkv, self.D, self.dtype_code,
-                k_st.data_ptr(), v_st.data_ptr(), pk.out_slots, current_stream_ptr(self.device),
+                "b2a_extend_groups", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), num_slots,
+                None if k_st is None else k_st.data_ptr(), None if v_st is None else v_st.data_ptr(), stage_slots,
+                meta.qo_indptr.data_ptr(), meta.kv_indptr.data_ptr(), meta.kv_indices.data_ptr(),
+                meta.kv_last_page_len.data_ptr(), meta.work.data_ptr(), meta.n_work, T, B, self.Hq, self.Hkv,
+                self.D, float(self.scale), out.data_ptr(), self.dtype_code, current_stream_ptr(self.device),
             )
-            k_pool, v_pool, num_slots = k_st, v_st, pk.out_slots
+            return out
         nat.call(
             "b2a_extend", q.data_ptr(), k_pool.data_ptr(), v_pool.data_ptr(), num_slots, meta.qo_indptr.data_ptr(),
             meta.kv_indptr.data_ptr(), meta.kv_indices.data_ptr(), meta.kv_last_page_len.data_ptr(),

@@ -105,7 +105,7 @@ def test_extend_config3_full_benchmark_batch(P):
     q = torch.randn((T, Hq, D), device="cuda", generator=gen).to(torch.bfloat16)
     be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=P)
     meta = be.extend_metadata_from_lens(pb.rows, pb.lens, eb.extend)
-    assert (meta.pack is not None) == (P == 1)
+    assert (meta.pack is not None) == (P == 1) and meta.group_starts == (P == 1)
     out = be._forward_prefill(q, None, None, 0, meta).float().cpu()
     torch.cuda.synchronize()
     idx = [pb.page_table[b, : int(pb.lens[b])] for b in range(pb.batch_size)]
@@ -114,6 +114,60 @@ def test_extend_config3_full_benchmark_batch(P):
     ref = O.forward_prefill_torch(q.cpu(), kv.k[0].cpu(), kv.v[0].cpu(), qo, idx, D ** -0.5)
     err = float((out.double() - ref).abs().max())
     assert err <= TOL["bfloat16"], err
+
+
+@pytest.mark.parametrize("hq,hkv", [(16, 8), (32, 8)])
+def test_extend_page1_runs_read_in_place_fragments_packed(hq, hkv):
+    """Page size 1, bf16 (b2a_extend_groups): 16-key groups that are one run of consecutive
+    slots are read in place, the others are packed into the staging pool first. The
+    requests mix the cases: one run from an unaligned slot, random slots, two runs that
+    meet inside a group, a run that ends at the pool's last slot (its last group's box
+    reaches past the pool), a fresh prompt, one query over a short run."""
+    rng = np.random.default_rng(11)
+    N = 6000
+    prefix = np.array([200, 150, 24, 40, 0, 16], np.int64)
+    extend = np.array([70, 33, 40, 5, 129, 1], np.int64)
+    lens = prefix + extend
+    free = rng.permutation(np.arange(2000, 5000))
+    table = np.zeros((len(lens), int(lens.max())), np.int32)
+    table[0, :270] = 37 + np.arange(270)
+    table[1, :183] = free[:183]
+    table[2, :64] = np.concatenate([400 + np.arange(24), 900 + np.arange(40)])
+    table[3, :45] = N - 45 + np.arange(45)
+    table[4, :129] = 1200 + np.arange(129)
+    table[5, :17] = 1500 + np.arange(17)
+    pb = W.PagedBatch(table, np.arange(len(lens)), lens, 1, N)
+    eb = W.ExtendBatch(pb, prefix, extend)
+    out, ref = _run_extend(eb, hq, hkv, 128, "bfloat16", seed=12)
+    err = max_abs(out, ref)
+    assert err <= TOL["bfloat16"], err
+
+
+def test_extend_page1_group_metadata():
+    """Which groups are read in place and where the packed ones start (host metadata)."""
+    import torch
+
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.kvcache import MHAKVCache
+
+    N = 1000
+    lens = np.array([40, 20, 16], np.int64)
+    table = np.zeros((3, 40), np.int32)
+    table[0, :40] = 37 + np.arange(40)
+    table[1, :20] = [5, 9, 3, 700, 701, 702, 703, 704, 705, 706, 707, 708, 709, 710, 711, 712, 800, 801, 802, 803]
+    table[2, :16] = np.concatenate([500 + np.arange(8), 600 + np.arange(8)])
+    kv = MHAKVCache(1, N, 8, 128, torch.bfloat16)
+    be = B200AttnBackend(HeadConfig(16, 8, 128), kv, table, page_size=1)
+    meta = be.extend_metadata_from_lens(np.arange(3), lens, np.array([4, 4, 4]))
+    assert meta.group_starts and meta.page_size == 16
+    np.testing.assert_array_equal(to_np(meta.kv_indptr), [0, 3, 5, 6])
+    # request 0: runs at 37, 53, 69 (the last of 8 keys); request 1: its first group is not a
+    # run (staging page 0), its 4-key tail is (800); request 2: two runs of 8 (staging page 1)
+    np.testing.assert_array_equal(to_np(meta.kv_indices), [37, 53, 69, N, 800, N + 16])
+    np.testing.assert_array_equal(to_np(meta.kv_last_page_len), [8, 4, 16])
+    pk = meta.pack
+    assert pk.n_groups == 2 and pk.out_slots == 32
+    np.testing.assert_array_equal(to_np(pk.src_kv_indices), np.concatenate([table[1, :16], table[2, :16]]))
 
 
 def test_extend_single_request_long_prefix_bf16():
@@ -155,3 +209,30 @@ def test_pack_kv_rows_bit_exact(P):
         assert np.array_equal(ko[dst], kp[src]) and np.array_equal(vo[dst], vp[src])
         tail = np.arange(opi[b] * 16 + L, opi[b + 1] * 16)
         assert not ko[tail].any() and not vo[tail].any()  # rows past the request stay untouched
+
+
+def test_pack_kv_row_list_bit_exact():
+    """b2a_pack_kv row-list form: staging row g = pool row kv_indices[g], byte for byte;
+    a source outside the pool is skipped (row left as it was) and reported."""
+    import torch
+
+    from minisgl_b200 import _native as nat
+
+    rng = np.random.default_rng(8)
+    Hkv, D, N = 8, 128, 4096
+    k_pool = torch.randn((N, Hkv, D), device="cuda").to(torch.bfloat16)
+    v_pool = torch.randn((N, Hkv, D), device="cuda").to(torch.bfloat16)
+    src = rng.integers(0, N, 48).astype(np.int32)
+    src[20] = N + 3  # outside the pool
+    k_out = torch.zeros((48, Hkv, D), dtype=torch.bfloat16, device="cuda")
+    v_out = torch.zeros_like(k_out)
+    s = torch.from_numpy(src).cuda()
+    nat.call("b2a_pack_kv", k_pool.data_ptr(), v_pool.data_ptr(), N, None, s.data_ptr(), 1, None, None, 3, 48, Hkv,
+             D, nat.B2A_DTYPE_BF16, k_out.data_ptr(), v_out.data_ptr(), 48, torch.cuda.current_stream().cuda_stream)
+    code = nat.ctypes.c_int(0)
+    nat.call("b2a_device_error", torch.cuda.current_stream().cuda_stream, nat.ctypes.byref(code))
+    assert code.value == 32
+    kp, vp, ko, vo = (t.view(torch.int16).cpu().numpy() for t in (k_pool, v_pool, k_out, v_out))
+    ok = np.arange(48) != 20
+    assert np.array_equal(ko[ok], kp[src[ok]]) and np.array_equal(vo[ok], vp[src[ok]])
+    assert not ko[20].any() and not vo[20].any()

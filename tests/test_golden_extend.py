@@ -15,8 +15,8 @@ Generator: tests/golden/make_golden_extend.py.
   extend), and -- where the reference checkout was built -- re-running the kernel
   reproduces stored rows bit for bit.
 * GPU: the backend's prefill path reproduces the stored rows at page size 16 (the
-  tcgen05 kernel for bf16, the SIMT kernel for fp32) and at page size 1 (the page
-  packer plus the tcgen05 kernel for bf16, the SIMT kernel for fp32).
+  tcgen05 kernel for bf16, the SIMT kernel for fp32) and at page size 1 (the tcgen05
+  kernel over 16-key groups for bf16, the SIMT kernel for fp32).
 """
 
 from __future__ import annotations
@@ -106,9 +106,9 @@ def test_cuda_extend_matches_reference_kernel(golden, hq, hkv, d, dt, P):
     be = B200AttnBackend(HeadConfig(hq, hkv, d), kv, table, page_size=P)
     lens = np.array(GE.PREFIX) + np.array(GE.EXTEND)
     meta = be.extend_metadata_from_lens(np.arange(len(lens)), lens, np.array(GE.EXTEND))
-    if dt == "bfloat16":  # the tensor-core kernel (through the packer at page size 1)
+    if dt == "bfloat16":  # the tensor-core kernel (over 16-key groups at page size 1)
         assert nat.extend_tile_q(hq, hkv, d, nat.B2A_DTYPE_BF16, 16) == 2 * 128 // (hq // hkv)
-        assert (meta.pack is not None) == (P == 1)
+        assert meta.group_starts == (P == 1)
     out = be._forward_prefill(to_dev(q, dt), None, None, 0, meta)
     torch.cuda.synchronize()
     got = _stored(to_np(out), rows, hq // hkv)
