@@ -278,14 +278,14 @@ __device__ __forceinline__ void decode_group(const T* __restrict__ kh, const T* 
 // other CTAs of the same launch: consumer warp w takes query heads w, w + NCW, ...
 // The rows are read through L2 (ld.global.cg): another SM wrote them, and this
 // SM's L1 may still hold lines of the same workspace from an earlier launch.
-// Up to four partials are fetched at once and folded into a running (M, l, acc)
+// Up to eight partials are fetched at once and folded into a running (M, l, acc)
 // (the same online rescaling as the kernel's softmax), so a merge costs one L2
-// round trip per four partials instead of a dependent load chain per partial.
+// round trip per eight partials instead of a dependent load chain per partial.
 template <typename T, int D>
 __device__ __forceinline__ void decode_merge_request(const DecodeArgs& a, int b, int p0, int p1, int warp,
                                                      int lane) {
   constexpr int EPT = D / 32;
-  constexpr int U = 4;  // partials fetched together: one L2 round trip per U partials
+  constexpr int U = 8;  // partials fetched together: one L2 round trip per U partials
   const int Hq = a.Hq;
   for (int qh = warp; qh < Hq; qh += a.NCW) {
     float M = kNegInf, Lsum = 0.f, acc[EPT];
@@ -341,7 +341,12 @@ __device__ __forceinline__ void decode_merge_request(const DecodeArgs& a, int b,
 
 template <typename T, int D, int G, int NCW>
 __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeArgs a) {
-  pdl_wait_then_release();
+  // Programmatic dependent launch: the next kernel may become resident now; this one
+  // sets up its barriers and reads its plan and the first stage's page ids while the
+  // previous kernel still runs, and waits for it (griddepcontrol.wait) only before
+  // touching what that kernel may have written: q, the KV rows, the workspace, out.
+  // The plan arrays are written before the previous kernel of the stream starts.
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   constexpr int EPT = D / 32;
   constexpr int TG = decode_tg<G>();
   constexpr int REM = 5 - ilog2c(TG * G);
@@ -386,6 +391,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
     const size_t rowB = a.row_bytes;
     int ctr = 0;
     bool ok = true;
+    bool waited = false;  // griddepcontrol.wait done (before the first copy)
     const bool last_first = decode_last_first(a, seg0, seg1);
     for (int i = 0; i < seg1 - seg0 && ok; ++i) {
       const int si = decode_seg_at(a, seg0, seg1, last_first, i);
@@ -459,6 +465,10 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
           else mbar_arrive(&full[st]);
         }
         __syncwarp();
+        if (!waited) {
+          asm volatile("griddepcontrol.wait;" ::: "memory");  // the KV rows of the previous kernel
+          waited = true;
+        }
         if (all_ok) {
 #pragma unroll
           for (int u = 0; u < 2; ++u) {
@@ -490,6 +500,7 @@ __global__ void __launch_bounds__((NCW + 1) * 32, 1) decode_kernel(const DecodeA
   volatile int* s_last = reinterpret_cast<volatile int*>(smem + L.last_flag);
   const T* qbase = reinterpret_cast<const T*>(a.q);
   int ctr = 0;
+  asm volatile("griddepcontrol.wait;" ::: "memory");  // q, the workspace and out follow the previous kernel
   const bool last_first = decode_last_first(a, seg0, seg1);
   for (int i = 0; i < seg1 - seg0; ++i) {
     const int si = decode_seg_at(a, seg0, seg1, last_first, i);
