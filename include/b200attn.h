@@ -158,6 +158,13 @@ int b2a_paged_decode(const void* q, const void* k_pool, const void* v_pool, int6
  * slot is outside its request's merge range (or past n_partials) is skipped
  * and reported as device error 35 (b2a_device_error); such a call can leave
  * counters set, so zero the workspace again before the next call.
+ * Launched with programmatic stream serialization: the kernel reads the plan
+ * (cta_indptr, segs, merge_indptr) and the page ids before it waits for the
+ * previous kernel of the stream, and q, the pools, the workspace and out only
+ * after. Write the plan and the page ids with a copy or a kernel ordered
+ * before that previous kernel, or with a kernel that does not trigger its
+ * dependents early (griddepcontrol.launch_dependents), such as
+ * b2a_decode_metadata.
  * ------------------------------------------------------------------------ */
 int b2a_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, int B,
                     int page_size, int num_ctas, int32_t* cta_indptr, int32_t* segs,
