@@ -959,8 +959,9 @@ namespace {
 // occupancy calculator's, cached per (kernel, warps).
 template <int NB, int A, int MODE, bool NORM>
 int proj_launch(const b2a::ProjArgs& a0, int grid, cudaStream_t st) {
-  // 512-thread CTAs cap a thread at 128 registers, too few for 64 token rows
-  constexpr int MAXW = NB == 8 ? 8 : 16;
+  // 512-thread CTAs cap a thread at 128 registers: too few for 64 token rows, for the
+  // paired SwiGLU tiles and for the normalised operand batches; those take 8 warps
+  constexpr int MAXW = (NB == 8 || A == 2 || NORM) ? 8 : 16;
   auto kern = b2a::proj_kernel<NB, A, MODE, NORM, MAXW>;
   using S = b2a::ProjSmem<NB, A>;
   const int kc = a0.K / 128;

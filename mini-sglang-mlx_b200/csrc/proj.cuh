@@ -160,31 +160,41 @@ __global__ void __launch_bounds__(MAXW * 32) proj_kernel(const ProjArgs a) {
 #pragma unroll
   for (int n = 0; n < NB; ++n) ss[n] = 0.f;
 
+  // The token rows of CB chunks are loaded (and normalised) together before the first
+  // MMA that needs the slab: the slab's wait is ordered asm, so loads placed after it
+  // would each start only once the previous chunk's MMAs were issued.
+  constexpr int CB = NB <= 4 ? 4 : 2;
   bool landed = false;
   for (int s = 0; s < a.kpw; ++s) {
     const int kb = (warp * a.kpw + s) * 128 + 8 * t;
 #pragma unroll
-    for (int c = 0; c < 4; ++c) {
-      const int k = kb + c * 32;
-      uint4 xv[NB];
+    for (int c0 = 0; c0 < 4; c0 += CB) {
+      uint4 xv[CB][NB];
 #pragma unroll
-      for (int n = 0; n < NB; ++n) {
-        const int tok = n * 8 + g;
-        xv[n] = tok < a.M ? *reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.ldx + k) : make_uint4(0, 0, 0, 0);
-      }
-      if constexpr (NORM) {
-        const uint4 nwv = *reinterpret_cast<const uint4*>(a.norm_w + k);
-        const float2 w0 = bf2_to_f2(nwv.x), w1 = bf2_to_f2(nwv.y), w2 = bf2_to_f2(nwv.z), w3 = bf2_to_f2(nwv.w);
+      for (int cc = 0; cc < CB; ++cc) {
+        const int k = kb + (c0 + cc) * 32;
 #pragma unroll
         for (int n = 0; n < NB; ++n) {
-          const float2 x0 = bf2_to_f2(xv[n].x), x1 = bf2_to_f2(xv[n].y), x2 = bf2_to_f2(xv[n].z),
-                       x3 = bf2_to_f2(xv[n].w);
-          ss[n] += x0.x * x0.x + x0.y * x0.y + x1.x * x1.x + x1.y * x1.y + x2.x * x2.x + x2.y * x2.y +
-                   x3.x * x3.x + x3.y * x3.y;
-          xv[n].x = f2_to_bf2(x0.x * w0.x, x0.y * w0.y);
-          xv[n].y = f2_to_bf2(x1.x * w1.x, x1.y * w1.y);
-          xv[n].z = f2_to_bf2(x2.x * w2.x, x2.y * w2.y);
-          xv[n].w = f2_to_bf2(x3.x * w3.x, x3.y * w3.y);
+          const int tok = n * 8 + g;
+          xv[cc][n] = tok < a.M ? *reinterpret_cast<const uint4*>(a.x + (size_t)tok * a.ldx + k) : make_uint4(0, 0, 0, 0);
+        }
+      }
+      if constexpr (NORM) {
+#pragma unroll
+        for (int cc = 0; cc < CB; ++cc) {
+          const uint4 nwv = *reinterpret_cast<const uint4*>(a.norm_w + kb + (c0 + cc) * 32);
+          const float2 w0 = bf2_to_f2(nwv.x), w1 = bf2_to_f2(nwv.y), w2 = bf2_to_f2(nwv.z), w3 = bf2_to_f2(nwv.w);
+#pragma unroll
+          for (int n = 0; n < NB; ++n) {
+            uint4& v = xv[cc][n];
+            const float2 x0 = bf2_to_f2(v.x), x1 = bf2_to_f2(v.y), x2 = bf2_to_f2(v.z), x3 = bf2_to_f2(v.w);
+            ss[n] += x0.x * x0.x + x0.y * x0.y + x1.x * x1.x + x1.y * x1.y + x2.x * x2.x + x2.y * x2.y +
+                     x3.x * x3.x + x3.y * x3.y;
+            v.x = f2_to_bf2(x0.x * w0.x, x0.y * w0.y);
+            v.y = f2_to_bf2(x1.x * w1.x, x1.y * w1.y);
+            v.z = f2_to_bf2(x2.x * w2.x, x2.y * w2.y);
+            v.w = f2_to_bf2(x3.x * w3.x, x3.y * w3.y);
+          }
         }
       }
       if (!landed) {
@@ -194,13 +204,17 @@ __global__ void __launch_bounds__(MAXW * 32) proj_kernel(const ProjArgs a) {
         landed = true;
       }
 #pragma unroll
-      for (int i = 0; i < A; ++i) {
-        const uint4 w0 = lds128(slab + (uint32_t)(i * 16 + g) * rb + (uint32_t)k * 2);
-        const uint4 w1 = lds128(slab + (uint32_t)(i * 16 + g + 8) * rb + (uint32_t)k * 2);
+      for (int cc = 0; cc < CB; ++cc) {
+        const int k = kb + (c0 + cc) * 32;
 #pragma unroll
-        for (int n = 0; n < NB; ++n) {
-          proj_mma(acc[i][n], w0.x, w1.x, w0.y, w1.y, xv[n].x, xv[n].y);
-          proj_mma(acc[i][n], w0.z, w1.z, w0.w, w1.w, xv[n].z, xv[n].w);
+        for (int i = 0; i < A; ++i) {
+          const uint4 w0 = lds128(slab + (uint32_t)(i * 16 + g) * rb + (uint32_t)k * 2);
+          const uint4 w1 = lds128(slab + (uint32_t)(i * 16 + g + 8) * rb + (uint32_t)k * 2);
+#pragma unroll
+          for (int n = 0; n < NB; ++n) {
+            proj_mma(acc[i][n], w0.x, w1.x, w0.y, w1.y, xv[cc][n].x, xv[cc][n].y);
+            proj_mma(acc[i][n], w0.z, w1.z, w0.w, w1.w, xv[cc][n].z, xv[cc][n].w);
+          }
         }
       }
     }
