@@ -70,7 +70,7 @@ def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float, rows: torch.Tensor | 
 PROJ_PLAIN, PROJ_RESIDUAL, PROJ_SWIGLU = 0, 1, 2
 PROJ_MAX_ROWS = 64  # token rows of one b2a_proj launch
 # steps the model runs through b2a_proj: measured over the 28 layers of Qwen3-0.6B (CUDA
-# graph, B200) the fused layer takes 14 / 26 / 50 us at 8 / 32 / 64 rows against 33 / 31 /
+# graph, B200) the fused layer takes 12 / 23 / 36 us at 8 / 32 / 64 rows against 33 / 31 /
 # 30 us for cuBLAS + separate norm and SwiGLU kernels (every CTA re-reads all token rows,
 # a cost that grows with the rows), so larger steps keep the library GEMMs
 FUSED_MAX_ROWS = 32
