@@ -254,59 +254,19 @@ class B200AttnBackend(BaseAttnBackend):
     PACK_PAGE = 16
 
     def _grouped_extend_metadata(self, qo_indptr, lens, src_indptr, src_indices, P, tile_q) -> B200PrefillMetadata:
-        """Extend metadata for a pool whose page size is below 16: request b's keys in groups
-        of 16 (b2a_extend_groups). A group whose 16 rows are one run of consecutive slots
-        (what a fresh free list hands a prompt) is read in place: its start is its first
-        slot. The other groups are packed into 16-row pages of a staging pool
-        (b2a_pack_kv, one page per group) and start at num_slots + 16 * page."""
+        """Extend metadata for a pool whose page size is below 16 (b2a_extend_groups): the
+        16-key groups of ``extend_key_groups``, their packed rows uploaded with the rest."""
         Q = self.PACK_PAGE
-        B = len(lens)
-        lens = np.asarray(lens, dtype=np.int64)
-        tok_indptr = np.zeros(B + 1, np.int64)
-        np.cumsum(lens, out=tok_indptr[1:])
-        T_kv = int(tok_indptr[-1])
-        if T_kv >= 2 ** 31:
-            raise ValueError("grouped extend: more than 2^31 KV rows in one batch")
-        req = np.repeat(np.arange(B), lens)
-        pos = np.arange(T_kv, dtype=np.int64) - tok_indptr[req]
-        src_indptr = np.asarray(src_indptr, dtype=np.int64)
-        src_indices = np.asarray(src_indices, dtype=np.int64)
-        tok = src_indices[src_indptr[req] + pos // P] * P + pos % P  # slot of every key, in key order
-        ngroups = (lens + Q - 1) // Q
-        group_indptr = np.zeros(B + 1, np.int64)
-        np.cumsum(ngroups, out=group_indptr[1:])
-        G = int(group_indptr[-1])
-        gid = group_indptr[req] + pos // Q
-        gfirst = np.zeros(G, np.int64)  # key index of each group's first key
-        gfirst[gid[pos % Q == 0]] = np.nonzero(pos % Q == 0)[0]
-        num_slots = self.kv_cache.num_tokens
-        greq = np.repeat(np.arange(B), ngroups)
-        glen_all = np.minimum(Q, lens[greq] - Q * (np.arange(G) - group_indptr[greq]))
-        run_ok = tok == tok[gfirst[gid]] + pos % Q
-        group_ok = np.logical_and.reduceat(run_ok, gfirst) if G else np.zeros(0, bool)
-        # a run is read in place only inside the pool: any other slot goes through the
-        # packer, whose bounds check reports it (a start >= num_slots means the staging pool)
-        group_ok &= (tok[gfirst] >= 0) & (tok[gfirst] + glen_all <= num_slots)
-        packed = np.nonzero(~group_ok)[0]
-        n_packed = len(packed)
-        starts = np.where(group_ok, tok[gfirst] if G else 0, 0).astype(np.int64)
-        starts[packed] = num_slots + Q * np.arange(n_packed, dtype=np.int64)
-        if G and starts.max() >= 2 ** 31:
-            raise ValueError("grouped extend: staging slots past 2^31")
-        lpl = np.where(ngroups > 0, lens - (ngroups - 1) * Q, 0).astype(np.int32)
-        group_indptr32 = group_indptr.astype(np.int32)
-        work = nat.extend_plan(qo_indptr, group_indptr32, lpl, Q, tile_q)
+        group_indptr, starts, lpl, rows = extend_key_groups(lens, src_indptr, src_indices, P,
+                                                            self.kv_cache.num_tokens, Q)
+        n_packed = len(rows) // Q
+        work = nat.extend_plan(qo_indptr, group_indptr, lpl, Q, tile_q)
         last_indices = (qo_indptr[1:] - 1).astype(np.int32)
-        arrays = [last_indices, qo_indptr, group_indptr32, starts.astype(np.int32), lpl, work]
-        pack = None
+        arrays = [last_indices, qo_indptr, group_indptr, starts, lpl, work]
         if n_packed:
-            # the packed groups' source slots as a row list of 16 per group (staging row
-            # 16 k + i); a short last group repeats its last slot in rows nobody attends
-            rows16 = gfirst[packed][:, None] + np.minimum(np.arange(Q)[None, :], glen_all[packed][:, None] - 1)
-            arrays.append(tok[rows16.reshape(-1)].astype(np.int32))
+            arrays.append(rows)
         dev = self._stager.upload(arrays, self.device)
-        if n_packed:
-            pack = PackPlan(src_kv_indices=dev[6], n_groups=n_packed, out_slots=Q * n_packed)
+        pack = PackPlan(src_kv_indices=dev[6], n_groups=n_packed, out_slots=Q * n_packed) if n_packed else None
         return B200PrefillMetadata(
             last_indices=dev[0], q_offsets=qo_indptr.tolist(), qo_indptr=dev[1], kv_indptr=dev[2],
             kv_indices=dev[3], kv_last_page_len=dev[4], work=dev[5].view(-1, 4), n_work=int(work.shape[0]),
@@ -361,6 +321,60 @@ class B200AttnBackend(BaseAttnBackend):
             float(self.scale), out.data_ptr(), self.dtype_code, current_stream_ptr(self.device),
         )
         return out
+
+
+def extend_key_groups(lens, src_indptr, src_indices, P: int, num_slots: int, Q: int = 16):
+    """Keys of every request in groups of Q = 16 for b2a_extend_groups, over a pool whose page
+    size P is below 16.
+
+    Group j of request b covers keys [16 j, 16 j + 16). A group whose slots are one run of
+    consecutive slots that lies wholly inside the pool (what a fresh free list hands a
+    prompt) is read in place: its start is its first slot. Every other group is packed into
+    a 16-row page of a staging pool, in group order, and starts at num_slots + 16 * page.
+
+    lens [B] keys per request; src_indptr [B+1] / src_indices the page CSR of the pool
+    (page ids, P slots each). Returns int32 arrays: group_indptr [B+1], starts [groups],
+    the key count of each request's last group [B] (0 for an empty request), and the
+    source slot of every staging row [16 * packed groups] (row 16 k + i of packed group k;
+    rows past a short last group repeat its last slot and are never attended).
+    """
+    lens = np.asarray(lens, dtype=np.int64)
+    B = len(lens)
+    tok_indptr = np.zeros(B + 1, np.int64)
+    np.cumsum(lens, out=tok_indptr[1:])
+    T_kv = int(tok_indptr[-1])
+    if T_kv >= 2 ** 31:
+        raise ValueError("grouped extend: more than 2^31 KV rows in one batch")
+    req = np.repeat(np.arange(B), lens)
+    pos = np.arange(T_kv, dtype=np.int64) - tok_indptr[req]
+    src_indptr = np.asarray(src_indptr, dtype=np.int64)
+    src_indices = np.asarray(src_indices, dtype=np.int64)
+    tok = src_indices[src_indptr[req] + pos // P] * P + pos % P  # slot of every key, in key order
+    ngroups = (lens + Q - 1) // Q
+    group_indptr = np.zeros(B + 1, np.int64)
+    np.cumsum(ngroups, out=group_indptr[1:])
+    G = int(group_indptr[-1])
+    gid = group_indptr[req] + pos // Q
+    gfirst = np.zeros(G, np.int64)  # key index of each group's first key
+    gfirst[gid[pos % Q == 0]] = np.nonzero(pos % Q == 0)[0]
+    greq = np.repeat(np.arange(B), ngroups)
+    glen = np.minimum(Q, lens[greq] - Q * (np.arange(G) - group_indptr[greq]))
+    run_ok = tok == tok[gfirst[gid]] + pos % Q
+    group_ok = np.logical_and.reduceat(run_ok, gfirst) if G else np.zeros(0, bool)
+    # a run is read in place only inside the pool: any other slot goes through the
+    # packer, whose bounds check reports it (a start >= num_slots means the staging pool)
+    if G:
+        group_ok &= (tok[gfirst] >= 0) & (tok[gfirst] + glen <= num_slots)
+    packed = np.nonzero(~group_ok)[0]
+    n_packed = len(packed)
+    starts = np.where(group_ok, tok[gfirst] if G else 0, 0).astype(np.int64)
+    starts[packed] = num_slots + Q * np.arange(n_packed, dtype=np.int64)
+    if G and starts.max() >= 2 ** 31:
+        raise ValueError("grouped extend: staging slots past 2^31")
+    lpl = np.where(ngroups > 0, lens - (ngroups - 1) * Q, 0).astype(np.int32)
+    rows = gfirst[packed][:, None] + np.minimum(np.arange(Q)[None, :], glen[packed][:, None] - 1)
+    return (group_indptr.astype(np.int32), starts.astype(np.int32), lpl,
+            tok[rows.reshape(-1)].astype(np.int32))
 
 
 def paged_decode_attention(q: torch.Tensor, k_pool: torch.Tensor, v_pool: torch.Tensor,
