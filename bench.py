@@ -67,6 +67,11 @@ def parse_args():
     ap.add_argument("--c4-requests", type=int, default=None,
                     help="config 4 with only its first N requests (one rank's share at N = 256/world)")
     ap.add_argument("--no-config4-shared", action="store_true", help="skip the shared-prefix config-4 line")
+    ap.add_argument("--proj-sweep", type=str, default=None, metavar="ROWS",
+                    help="only time the 28 layers' projections of Qwen3-0.6B at these token counts "
+                         "(comma list), fused b2a_proj against cuBLAS + b2a_rmsnorm + b2a_swiglu")
+    ap.add_argument("--decode-sweep", type=str, default=None, metavar="BATCHES",
+                    help="only time one decode call of config-2 shapes at these batch sizes (comma list)")
     ap.add_argument("--no-fused-proj", action="store_true",
                     help="config 4 with the unfused projections (cuBLAS GEMMs + separate norm / SwiGLU kernels)")
     ap.add_argument("--c5-requests", type=int, default=None,
@@ -939,9 +944,120 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def graph_time_ms(fn, reps: int) -> float:
+    """Device time of one call of fn: reps calls captured in one CUDA graph, CUDA events around
+    replays, the median over 5 replays divided by reps."""
+    import torch
+
+    fn()
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(s), torch.cuda.graph(g, stream=s):
+        for _ in range(reps):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    g.replay()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(5):
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        torch.cuda.synchronize()
+        times.append(a.elapsed_time(b))
+    return float(np.median(times)) / reps
+
+
+def proj_sweep(rows_list):
+    """The decode-step projections of the engine harness's model over its 28 layers.
+
+    Per layer: RMSNorm + qkv_proj, o_proj + residual, RMSNorm + gate_up_proj + SwiGLU,
+    down_proj + residual (models/transformer.py:80-82), either as four b2a_proj launches or as
+    cuBLAS GEMMs with the residual adds folded in (addmm) plus b2a_rmsnorm and b2a_swiglu.
+    Random weights; 28 x 30 MB of weights > L2. One JSON line per token count.
+    """
+    import torch
+    import torch.nn.functional as F
+
+    from minisgl_b200.engine.model import PROJ_PLAIN, PROJ_RESIDUAL, PROJ_SWIGLU, proj, rms_norm, swiglu
+
+    dev = torch.device("cuda", 0)
+    Lyr, H, I, QKV, O = 28, 1024, 3072, 4096, 2048
+    gen = torch.Generator(device=dev).manual_seed(0)
+
+    def w(o, i):
+        return (torch.randn((o, i), device=dev, generator=gen) * 0.02).to(torch.bfloat16)
+
+    layers = [dict(qkv=w(QKV, H), o=w(H, O), gu=w(2 * I, H), d=w(H, I)) for _ in range(Lyr)]
+    ones = torch.ones(H, device=dev, dtype=torch.bfloat16)
+    wbytes = sum(x.numel() * 2 for lw in layers for x in lw.values())
+    peak, kind = measured_peaks()
+    for M in rows_list:
+        h = torch.randn((M, H), device=dev, generator=gen).to(torch.bfloat16)
+        attn = torch.randn((M, O), device=dev, generator=gen).to(torch.bfloat16)
+
+        def fused():
+            for lw in layers:
+                proj(h, lw["qkv"], PROJ_PLAIN, ones, 1e-6)
+                proj(attn, lw["o"], PROJ_RESIDUAL, res=h, out=h)
+                proj(proj(h, lw["gu"], PROJ_SWIGLU, ones, 1e-6), lw["d"], PROJ_RESIDUAL, res=h, out=h)
+
+        def unfused():
+            x = h
+            for lw in layers:
+                F.linear(rms_norm(x, ones, 1e-6), lw["qkv"])
+                x = torch.addmm(x, attn, lw["o"].t())
+                x = torch.addmm(x, swiglu(F.linear(rms_norm(x, ones, 1e-6), lw["gu"])), lw["d"].t())
+
+        line = {"metric": "engine projections, 28 layers of Qwen3-0.6B (us per layer, CUDA graph)", "rows": M,
+                "weight_bytes_per_layer": wbytes // Lyr, "hbm_us_per_layer": round(wbytes / Lyr / (peak * 1e3), 2)}
+        for name, fn in (("fused", fused), ("unfused", unfused)):
+            ms = graph_time_ms(fn, 3)
+            line[name] = {"us_per_layer": round(ms * 1e3 / Lyr, 2), "weight_gbs": round(wbytes / (ms * 1e-3) / 1e9, 1)}
+        print(json.dumps(line), flush=True)
+
+
+def decode_sweep(batches):
+    """One decode call (config-2 shapes: 16q/8kv/128, bf16, page 16, L~U[100,2048]) per batch
+    size, replayed 20 at a time in a CUDA graph. One JSON line per batch size."""
+    import torch
+
+    from minisgl_b200 import MHAKVCache
+    from minisgl_b200 import workloads as W
+    from minisgl_b200.attention import B200AttnBackend
+    from minisgl_b200.config import qwen3_0_6b
+
+    dev = torch.device("cuda", 0)
+    cfg = qwen3_0_6b()
+    N = W.CONFIG2["num_slots"]
+    kv = MHAKVCache(1, N, 8, 128, torch.bfloat16, device=dev)
+    gen = torch.Generator(device=dev).manual_seed(0)
+    kv.k[0].normal_(generator=gen)
+    kv.v[0].normal_(generator=gen)
+    peak, kind = measured_peaks()
+    for B in batches:
+        pb = W.config2_batch(seed=1, batch=B)
+        be = B200AttnBackend(cfg, kv, pb.page_table, page_size=16)
+        meta = be.decode_metadata_from_lens(pb.rows, pb.lens)
+        q = torch.randn((B, 16, 128), device=dev, generator=gen).to(torch.bfloat16)
+        ms = graph_time_ms(lambda: be.forward_decode(q, 0, meta), 20)
+        nbytes = decode_bytes(pb.lens, 16, 16, 8, 128, 2)
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        print(json.dumps({"metric": "decode call, config-2 shapes (CUDA graph)", "batch": B,
+                          "sum_ctx_tokens": int(pb.lens.sum()), "bytes_per_call": nbytes, "us_per_call": round(ms * 1e3, 2),
+                          "gbs": round(gbs, 1), "frac": round(gbs / peak, 4), "peak_kind": kind}), flush=True)
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.proj_sweep:
+        proj_sweep([int(x) for x in args.proj_sweep.split(",")])
+    elif args.decode_sweep:
+        decode_sweep([int(x) for x in args.decode_sweep.split(",")])
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_ours(args)
