@@ -135,7 +135,9 @@ int b2a_paged_decode(const void* q, const void* k_pool, const void* v_pool, int6
  * forward_decode (attention/naive.py:50-60), which computes the same values.
  *
  * b2a_decode_plan (host only, no GPU): cuts the concatenated page stream of
- * all requests into `num_ctas` near-equal contiguous ranges. Each range is a
+ * all requests into `num_ctas` near-equal contiguous ranges of at least 64
+ * tokens' worth of pages each (a small batch leaves the last CTAs without
+ * work rather than splitting every page into its own partial). Each range is a
  * list of segments {request, first page index into kv_indices, n_tokens,
  * out_slot}; out_slot == -1 writes the final output directly, otherwise the
  * segment writes a partial (m, l, acc) that b2a_decode merges per request.

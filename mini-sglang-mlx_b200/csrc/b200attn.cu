@@ -347,7 +347,7 @@ int b2a_decode_plan(const int32_t* kv_indptr, const int32_t* kv_last_page_len, i
       return fail(B2A_ERR_INVALID, "kv_last_page_len[%d]=%d out of [1, %d]", b, kv_last_page_len[b], page_size);
   }
   const int64_t total = kv_indptr[B];
-  const int64_t per = std::max<int64_t>(1, (total + num_ctas - 1) / num_ctas);
+  const int64_t per = b2a::decode_share_pages(total, num_ctas, ilog2_exact(page_size));
   int ns = 0, np = 0;
   std::fill(cta_indptr, cta_indptr + num_ctas + 1, 0);
   std::vector<int> seg_cta;

@@ -10,8 +10,8 @@
 //
 //   decode_plan_kernel   one CTA: npages scan -> kv_indptr, last_page_len;
 //                        pieces of every request (cuts at multiples of
-//                        ceil(total / num_ctas) pages, the last CTA takes the
-//                        rest) -> segs, merge_indptr; segment histogram per
+//                        decode_share_pages(total, num_ctas) pages, the last
+//                        CTA takes the rest) -> segs, merge_indptr; segment histogram per
 //                        CTA -> cta_indptr. Same arithmetic as
 //                        b2a_decode_plan, so the outputs are identical.
 //   decode_indices_kernel  kv_indices[kv_indptr[b] + p] = page_table[row_b, p * P] / P.
@@ -27,6 +27,18 @@ namespace b2a {
 
 constexpr int kPlanThreads = 1024;
 constexpr int kPlanMaxCtas = 1024;
+
+// Pages of one CTA's share of a decode batch: the batch's pages over the CTAs, but never
+// fewer than 64 tokens' worth. A tiny batch then runs on fewer CTAs with fewer split
+// partials to merge (the merge reads them in a handful of L2 round trips), instead of one
+// partial per page across the whole grid. Host and device plans use this one formula.
+constexpr int kDecodeMinShareTokens = 64;
+
+__host__ __device__ inline int64_t decode_share_pages(int64_t total, int num_ctas, int page_log2) {
+  const int64_t floor_pages = page_log2 >= 6 ? 1 : (int64_t)(kDecodeMinShareTokens >> page_log2);
+  const int64_t even = (total + num_ctas - 1) / num_ctas;
+  return even > floor_pages ? even : floor_pages;
+}
 
 struct DecodeMetaArgs {
   const int32_t* page_table;
@@ -107,7 +119,7 @@ __global__ void __launch_bounds__(kPlanThreads, 1) decode_plan_kernel(const Deco
   if (threadIdx.x == 0) a.kv_indptr[a.B] = carry;
   __syncthreads();
   const int64_t total = carry;
-  const int64_t per = max((int64_t)1, (total + C - 1) / C);
+  const int64_t per = decode_share_pages(total, C, a.page_log2);
   // ---- pieces, segments, merge ranges
   int seg_carry = 0, part_carry = 0;
   if (threadIdx.x == 0) a.merge_indptr[0] = 0;

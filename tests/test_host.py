@@ -92,8 +92,8 @@ def test_decode_plan_covers_every_page_once(num_ctas, P):
         assert n == (pieces if pieces > 1 else 0)
     used = [s for s in slots_seen if s >= 0]
     assert sorted(used) == list(range(n_part))
-    # balance: no CTA holds more than ceil(total/num_ctas) pages
-    per = -(-int(ind[-1]) // num_ctas)
+    # balance: no CTA holds more than ceil(total/num_ctas) pages, or 64 tokens' worth
+    per = max(-(-int(ind[-1]) // num_ctas), max(1, 64 // P))
     for c in range(num_ctas):
         pages = 0
         for b, pbeg, ntok, _ in segs[cta_indptr[c]:cta_indptr[c + 1]].tolist():
