@@ -101,6 +101,22 @@ def test_decode_plan_covers_every_page_once(num_ctas, P):
         assert pages <= per + 1
 
 
+@pytest.mark.parametrize("P", [1, 16])
+def test_decode_plan_minimum_share_for_tiny_batches(P):
+    """A CTA's share is at least 64 tokens' worth of pages: one request of 1024 tokens over
+    148 CTAs becomes 1024 / 64 = 16 pieces (not one partial per page); a batch large enough
+    for 148 shares of 64 tokens is cut as before."""
+    pages = 1024 // P
+    ind = np.array([0, pages], np.int32)
+    cta_indptr, segs, merge_indptr, n_part = nat.decode_plan(ind, None, P, 148)
+    assert n_part == 16 and len(segs) == 16
+    assert (np.diff(cta_indptr)[:16] == 1).all() and (np.diff(cta_indptr)[16:] == 0).all()
+    assert all(ntok == 64 for _, _, ntok, _ in segs.tolist())
+    big = 148 * 2 * 64 // P  # two minimum shares per CTA
+    cta_indptr, segs, _, n_part = nat.decode_plan(np.array([0, big], np.int32), None, P, 148)
+    assert len(segs) == 148 and n_part == 148
+
+
 def test_decode_plan_rejects_bad_input():
     with pytest.raises(ValueError, match="monotonic"):
         nat.decode_plan(np.array([0, 5, 3], np.int32), None, 1, 4)
