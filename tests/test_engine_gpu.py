@@ -59,6 +59,50 @@ def test_engine_fp32_tokens_match_oracle(overlap, graphs, device_meta):
     llm.engine.shutdown()
 
 
+# The engine configurations of the reference's end-to-end parity test (tests/test_e2e.py:40-46)
+# that do not name one of its MLX backends, plus its default page size 1 (engine/config.py:12).
+REFERENCE_E2E_CONFIGS = {
+    "chunked_prefill_16": dict(max_extend_tokens=16),
+    "page_size_4": dict(page_size=4),
+    "page_size_1": dict(page_size=1),
+    "naive_cache": dict(cache_type="naive"),
+}
+
+
+@pytest.mark.parametrize("name", list(REFERENCE_E2E_CONFIGS))
+def test_engine_fp32_reference_e2e_configs_two_rounds(name):
+    """As the reference's test_greedy_matches_mlx_lm (tests/test_e2e.py:49-58): each config
+    generates the same prompts twice, the second round served from the radix cache where
+    there is one, and both rounds' greedy tokens equal the float64 recompute oracle."""
+    import torch
+
+    from minisgl_b200.core import SamplingParams
+    from minisgl_b200.engine import LLM, EngineConfig, tiny_spec
+    from oracle.engine import OracleQwen3
+
+    rng = np.random.default_rng(6)
+    prompts = _prompts(rng)
+    max_tokens = [int(x) for x in rng.integers(8, 20, len(prompts))]
+    base = dict(spec=tiny_spec(num_layers=2, vocab_size=500), dtype="float32", max_running_req=4, page_size=16,
+                num_tokens=8192, max_extend_tokens=256, cuda_graph_max_bs=4)
+    llm = LLM(EngineConfig(**{**base, **REFERENCE_E2E_CONFIGS[name]}))
+    want = OracleQwen3(llm.engine.model).generate(prompts, max_tokens)
+    hits = []
+    for round_ in range(2):
+        before = llm.num_prefix_hit_tokens
+        outs = llm.generate(prompts, [SamplingParams(max_tokens=n, ignore_eos=True) for n in max_tokens])
+        torch.cuda.synchronize()
+        assert [o["token_ids"] for o in outs] == want, (name, round_)
+        hits.append(llm.num_prefix_hit_tokens - before)
+    if name == "naive_cache":
+        assert hits == [0, 0]
+    else:
+        assert hits[1] > hits[0]  # the second round reuses the first round's prompts
+    llm.cache.check_integrity()
+    assert llm.table.available_size == 4
+    llm.engine.shutdown()
+
+
 def test_engine_bf16_config4_shape_runs_clean():
     import ctypes
 
