@@ -18,21 +18,26 @@ pytestmark = pytest.mark.gpu
 
 
 def _run_extend(eb: W.ExtendBatch, Hq, Hkv, D, dtype, seed=0):
+    pb = eb.paged
+    rng = np.random.default_rng(seed)
+    N = pb.num_slots
+    hk = rand(rng, (N, Hkv, D), dtype)
+    hv = rand(rng, (N, Hkv, D), dtype)
+    q = rand(rng, (int(eb.extend.sum()), Hq, D), dtype)
+    return _run_extend_arrays(eb, Hq, Hkv, D, dtype, hk, hv, q)
+
+
+def _run_extend_arrays(eb: W.ExtendBatch, Hq, Hkv, D, dtype, hk, hv, q):
     import torch
 
     from minisgl_b200.attention import B200AttnBackend
     from minisgl_b200.kvcache import MHAKVCache
 
     pb = eb.paged
-    rng = np.random.default_rng(seed)
     N = pb.num_slots
-    hk = rand(rng, (N, Hkv, D), dtype)
-    hv = rand(rng, (N, Hkv, D), dtype)
     kv = MHAKVCache(1, N, Hkv, D, torch_dtype(dtype))
     kv.k[0].copy_(torch.from_numpy(hk))
     kv.v[0].copy_(torch.from_numpy(hv))
-    T = int(eb.extend.sum())
-    q = rand(rng, (T, Hq, D), dtype)
     be = B200AttnBackend(HeadConfig(Hq, Hkv, D), kv, pb.page_table, page_size=pb.page_size)
     meta = be.extend_metadata_from_lens(pb.rows, pb.lens, eb.extend)
     out = be._forward_prefill(to_dev(q, dtype), None, None, 0, meta)
@@ -70,6 +75,54 @@ def test_extend_edge_cases(hq, hkv, d, dtype, P):
     out, ref = _run_extend(eb, hq, hkv, d, dtype, seed=2)
     err = max_abs(out, ref)
     assert err <= TOL[dtype], err
+
+
+def _max_jumps(s2: np.ndarray, block: int = 128) -> list:
+    """How far each 128-key block's max rises above the running max before it, in log2
+    units, for one query row whose visible scores (s * scale * log2 e) are s2: the factor
+    2^-jump by which the tcgen05 extend rescales O and the row sum when a jump passes 8."""
+    jumps, m = [], float(s2[:block].max())
+    for j in range(1, -(-len(s2) // block)):
+        mb = float(s2[j * block:(j + 1) * block].max())
+        jumps.append(mb - m)
+        m = max(m, mb)
+    return jumps
+
+
+def test_extend_score_jumps_across_key_blocks():
+    """bf16 tcgen05 extend with planted key spikes that make a later key block score far
+    above the earlier ones, so that O and the row sum are rescaled by 2^-33, by 2^-16 then
+    2^-49, and by a factor below fp32's normal range (2^-130, which flushes the earlier terms to zero),
+    against the float64 oracle. q is all ones and every head of a spike key is a * ones,
+    so a spike scores 128 a / sqrt(128) * log2 e; the other keys score near 0."""
+    Hq, Hkv, D, P = 16, 8, 128, 16
+    prefix, extend = [272, 272, 400, 16], [24, 24, 24, 150]
+    spikes = [{150: 1.875, 200: 2.0},  # block 1 at 32.6, a second spike 2 below it
+              {150: 1.875, 200: 8.0},  # block 1 at 130.6
+              {150: 1.0, 300: 4.0, 340: 3.875},  # block 1 at 16.3, block 2 at 65.3 (49 above it)
+              {}]
+    eb = _batch(prefix, extend, P, seed=3)
+    pb = eb.paged
+    rng = np.random.default_rng(8)
+    N = pb.num_slots
+    hk = O.round_to(rand(rng, (N, Hkv, D), "bfloat16") * np.float32(2.0 ** -6), "bfloat16")
+    hv = rand(rng, (N, Hkv, D), "bfloat16")
+    T = int(eb.extend.sum())
+    q = np.ones((T, Hq, D), np.float32)
+    q[T - extend[-1]:] = rand(rng, (extend[-1], Hq, D), "bfloat16")
+    for b, sp in enumerate(spikes):
+        for pos, a in sp.items():
+            hk[pb.page_table[b, pos]] = np.float32(a)
+    # the inputs make the jumps they are meant to (row 0 of each request, head 0)
+    l2e = D ** -0.5 * np.log2(np.e)
+    biggest = []
+    for b in range(3):
+        s2 = (hk[pb.page_table[b, : int(prefix[b]) + 1], 0] @ q[int(np.sum(extend[:b])), 0]) * l2e
+        biggest.append(max(_max_jumps(s2)))
+    assert 32 < biggest[0] < 33 and biggest[1] > 126 and 48 < biggest[2] < 50, biggest
+    out, ref = _run_extend_arrays(eb, Hq, Hkv, D, "bfloat16", hk, hv, q)
+    err = max_abs(out, ref)
+    assert err <= TOL["bfloat16"], err
 
 
 @pytest.mark.parametrize("dtype", ["float32", "bfloat16"])
